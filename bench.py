@@ -1,0 +1,298 @@
+#!/usr/bin/env python
+"""bench.py: MoE-layer tokens/s of the B200 routed-MoE block (libqengine_b200) vs the reference C engine.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2]
+
+One step = one forward of one MoE block over the configuration's token batch (config c2: 512 tokens of the
+4-bit hidden-2048 block, the configuration the benchmark metric is quoted on). Four blocks with distinct
+weights (4 x 453 MB, far above the 126 MB L2) are used in rotation, so no step finds its weights in L2.
+`value` is device-timed (CUDA events on the launching stream, inputs resident in HBM); `e2e` is the same
+metric through the public host-buffer call qe_moe_forward (pinned host x in, host out back, every step).
+Under torchrun every rank runs its own replica (weak scaling); value = tokens of all ranks / max rank time.
+--impl reference times the reference's own C engine (oracle/_ref, built from its sources) on the host.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "moe-stream-mac_b200"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "MoE-layer tokens/s"
+PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def hbm_peak():
+    try:
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms while the timed region runs."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "50", "-i", str(gpu)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.p = None
+        self.t0 = self.t1 = None
+
+    def mark(self, start: bool):
+        if start:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.12)
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        rows = [r.split(", ") for r in Path(self.f.name).read_text().splitlines() if r.count(",") >= 9]
+        os.unlink(self.f.name)
+        samples, all_rows = [], []
+        for r in rows:
+            try:
+                ts = time.mktime(time.strptime(r[0].split(".")[0], "%Y/%m/%d %H:%M:%S")) + float("0." + r[0].split(".")[1])
+            except Exception:
+                continue
+            all_rows.append(r)
+            if self.t0 is not None and self.t0 - 0.06 <= ts <= (self.t1 or ts) + 0.06:
+                samples.append(r)
+        use = samples or all_rows[-3:]
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[2]) for r in use]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in use:
+            for n, v in zip(names, r[6:10]):
+                if v.strip() == "Active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(use[0][3]), "reasons": sorted(reasons),
+                "samples": len(samples), "power_w_max": max(float(r[4]) for r in use)}
+
+
+def reference_block(cfg, seed, threads):
+    import oracle as O
+    if not O.ref_available():
+        return None, None
+    O.ref().ref_set_threads(threads)
+    blk = O.SynthBlock(O.BlockCfg(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size),
+                       seed)
+    return O, blk
+
+
+def time_reference(cfg, seed, sample_tokens, steps, warmup, threads, budget_s=None):
+    """Reference C engine (Mode B harness over the reference's own qmat_matvec/op_* from oracle/_ref):
+    tokens one after the other, as the engine's prefill does; OpenMP inside qmat_matvec."""
+    O, blk = reference_block(cfg, seed, threads)
+    if blk is None:
+        return None
+    x = blk.x(sample_tokens)
+    for _ in range(warmup):
+        blk.forward_ref(x[:1])
+    times, done = [], 0
+    t_all = time.perf_counter()
+    for _ in range(steps):
+        t = time.perf_counter()
+        blk.forward_ref(x)
+        times.append(time.perf_counter() - t)
+        done += 1
+        if budget_s and time.perf_counter() - t_all > budget_s:
+            break
+    blk.close()
+    sec = sum(times)
+    return {"value": done * sample_tokens / sec, "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": f"{done} x {sample_tokens} tokens of {cfg.name} through the reference's moe_layer_step "
+                      f"restated around its own qmat_matvec/op_softmax/op_topk/op_silu_mul (oracle/_ref), "
+                      f"{threads} OpenMP threads, experts in RAM"}
+
+
+def run_reference_arm(args, cfg):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    res = time_reference(cfg, 1, args.ref_tokens, args.steps, min(args.warmup, 3), threads, budget_s=150)
+    if res is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libqref.so (reference build) is missing"}))
+        return
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.ref_tokens / res["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(cfg, world), "cpu_baseline": res,
+            "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def workload_config(cfg, world):
+    return {"workload": f"{cfg.name}: {cfg.note}", "tokens_per_step": cfg.tokens, "hidden": cfg.hidden,
+            "experts": cfg.E, "top_k": cfg.top_k, "inter": cfg.inter, "sh_inter": cfg.sh_inter, "bits": cfg.bits,
+            "group_size": cfg.group_size, "router": "fp32", "parallelism": "1 GPU" if world == 1 else
+            f"{world} independent replicas", "l2": "4 blocks with distinct weights rotated per step "
+                                                   f"({4 * 453} MB of weights > 126 MB L2)"}
+
+
+def stage_bytes(cfg, uniq: int, T: int) -> dict:
+    """Algorithmic bytes per launch of each expert kernel: every active expert's weights once, plus the
+    activations the kernel must read and write (fp32)."""
+    def q(rows, cols):
+        return rows * cols * cfg.bits // 8 + 4 * rows * (cols // cfg.group_size)
+    npair = T * (cfg.top_k + 1)
+    I = max(cfg.inter, cfg.sh_inter)
+    gu = uniq * 2 * q(cfg.inter, cfg.hidden) + 2 * q(cfg.sh_inter, cfg.hidden) + 4 * T * cfg.hidden + 4 * npair * I
+    dn = uniq * q(cfg.hidden, cfg.inter) + q(cfg.hidden, cfg.sh_inter) + 4 * npair * I + 4 * npair * cfg.hidden
+    return {"gateup": gu, "down": dn}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2")
+    ap.add_argument("--blocks", type=int, default=4)
+    ap.add_argument("--ref-tokens", type=int, default=16)
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    from qmoe.synth import CONFIGS
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference_arm(args, cfg)
+        return
+
+    import torch
+    import qmoe
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    T = cfg.tokens
+    blocks = [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size,
+                            max_tokens=T, device=local, seed=1000 * rank + b + 1, block=b)
+              for b in range(args.blocks)]
+    gen = torch.Generator(device="cuda").manual_seed(7 + rank)
+    x = torch.randn(T, cfg.hidden, device="cuda", generator=gen, dtype=torch.float32)
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+
+    def step(i):
+        blocks[i % len(blocks)].forward_device(T, x.data_ptr(), out.data_ptr(), sptr)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    clocks = ClockSampler(local)
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    barrier()
+    launches0 = qmoe.kernel_launches()
+    qmoe.profile_begin(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark(True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    barrier()
+    clocks.mark(False)
+    launches = qmoe.kernel_launches() - launches0
+    stage_ms, passes = qmoe.profile_end(local)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * T * args.steps / (ms_max / 1e3)
+
+    # end to end through the public host-buffer call: pinned host x in, host out back, every step
+    xh = torch.randn(T, cfg.hidden, generator=torch.Generator().manual_seed(11 + rank)).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    xn, on = xh.numpy(), oh.numpy()
+    ke = max(10, min(args.steps, 200))
+    for i in range(3):
+        blocks[i % len(blocks)].forward(xn, on)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(ke):
+        blocks[i % len(blocks)].forward(xn, on)
+    barrier()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+    e2e_value = world * T * ke / float(te.item())
+
+    # roofline of the dominant kernel (per-stage CUDA events recorded inside the timed region)
+    idx, _ = blocks[0].route(x.cpu().numpy())
+    uniq = len(np.unique(idx))
+    sb = stage_bytes(cfg, uniq, T)
+    top = max(("gateup", "down"), key=lambda s: stage_ms[s])
+    per_launch_ms = stage_ms[top] / max(passes, 1)
+    achieved = sb[top] / (per_launch_ms / 1e3) / 1e9
+    peak, peak_kind = hbm_peak()
+    total_stage = sum(stage_ms.values())
+    roofline = {"bound": "hbm", "kernel": f"expert_kernel<{cfg.bits},{cfg.group_size},{top}>", "achieved": achieved,
+                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else
+                "fallback 6.65 TB/s", "algorithmic_bytes_per_launch": sb[top], "unique_experts": uniq,
+                "stage_share": {k: round(v / total_stage, 4) for k, v in stage_ms.items()},
+                "stage_ms_per_pass": {k: round(v / max(passes, 1), 5) for k, v in stage_ms.items()}}
+
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(cfg, world),
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * cfg.hidden,
+                    "d2h_bytes_per_step": 4 * T * cfg.hidden, "steps": ke, "timing": "host clock, max over ranks"},
+            "roofline": roofline, "gpu_launches": launches, "clocks": clk}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = time_reference(cfg, 1, args.ref_tokens, 1000, 1, os.cpu_count() or 1, budget_s=args.cpu_budget)
+        line["cpu_baseline"] = cb if cb else {"value": None, "unavailable": "oracle/_ref missing"}
+    for b in blocks:
+        b.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

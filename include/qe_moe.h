@@ -1,0 +1,126 @@
+/* qe_moe.h: C ABI of libqengine_b200, the B200 routed-MoE block (one qwen3_5_moe sparse MoE layer).
+ *
+ * Drop-in boundary. In hatim-mlf/moe-stream-mac the block is
+ *     int moe_layer_step(float *out, const float *x, const MoeWeights *w, float *scratch);
+ * (engine/include/moe_layer.h:33, implemented at engine/src/moe_layer.c:66-89), called once per token and
+ * layer by model.c:layer_step (model.c:135-148) and, through the engine's C API (engine/include/qengine.h),
+ * by engine/cli/qchat.py via ctypes. This header is the same operation as a handle-based library in the
+ * conventions of that C API: opaque handle, NULL on a failed load with the reason on stderr, int return
+ * codes 0 = ok / -1 = error with outputs untouched, caller-owned input/output buffers, library-owned
+ * weights. The experts stay resident in HBM (the reference preads the 8 selected experts from SSD per
+ * token, engine/src/expert_store.c:54-61). There is no CPU fallback: without a usable GPU, create returns
+ * NULL.
+ *
+ * Threading: a handle is not thread-safe. All handles on one device share one scratch workspace and one
+ * stream for the host-buffer calls, so calls must not overlap (the reference is single-caller too).
+ */
+#ifndef QE_MOE_H
+#define QE_MOE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct QeMoe QeMoe;
+
+enum { QE_ROUTER_F32 = 0, QE_ROUTER_QMAT = 1 };
+
+/* Block shape: the MoeWeights fields of engine/include/moe_layer.h:19-20 plus the experts' affine
+ * quantization (bits 4 or 8, group_size 32/64/128: engine/src/qmat.c:16-20) and the router kind. */
+typedef struct {
+    int hidden, E, top_k, inter, sh_inter;
+    int bits, group_size;
+    int router_mode;      /* QE_ROUTER_F32: fp32 router [E][hidden] + fp32 shared gate [hidden];
+                             QE_ROUTER_QMAT: quantized router QMat [E][hidden] + shared gate QMat [1][hidden]
+                             (the checkpoint layout, moe_layer.h:13 and :18) */
+    int router_bits;      /* bits of the quantized router (QE_ROUTER_QMAT) */
+    int max_tokens;       /* tokens per internal pass (scratch sizing); forward accepts any T >= 1 */
+    int device;           /* CUDA device ordinal */
+    int layer;            /* layer id written to the QE_TRACE routing trace (moe_layer.c:57-64) */
+} QeMoeConfig;
+
+/* One quantized tensor in the MLX affine layout (engine/include/qmat.h:3-11): uint32 codes
+ * [n][rows][cols*bits/32] (LSB first), bf16 scales and biases [n][rows][cols/group_size]. */
+typedef struct {
+    const uint32_t *w;
+    const uint16_t *scales;
+    const uint16_t *biases;
+} QeQTensor;
+
+/* Host pointers to one block's weights (MoeWeights, moe_layer.h:12-21; names of model.c:52-64). */
+typedef struct {
+    const float *router_f32;   /* [E][hidden]                      (QE_ROUTER_F32)  */
+    const float *router_bias;  /* [E] added to the fp32 logits, or NULL                */
+    const float *sh_gate_f32;  /* [hidden]                          (QE_ROUTER_F32)  */
+    QeQTensor router_q;        /* mlp.gate            [E][hidden]  (QE_ROUTER_QMAT) */
+    QeQTensor sh_router_q;     /* mlp.shared_expert_gate [1][hidden] (QE_ROUTER_QMAT) */
+    QeQTensor gate, up, down;  /* mlp.switch_mlp.{gate,up,down}_proj [E][...]          */
+    QeQTensor sh_gate, sh_up, sh_down; /* mlp.shared_expert.{gate,up,down}_proj        */
+} QeMoeWeights;
+
+/* Validate cfg, copy the weights into HBM. NULL on failure (stderr says why). Replaces load_moe
+ * (engine/src/model.c:52-82) + expert_tensor_open (engine/src/expert_store.c:21-36). */
+QeMoe *qe_moe_create(const QeMoeConfig *cfg, const QeMoeWeights *w);
+
+/* Same block generated directly in HBM from the seeded generator of csrc/synth.h (bit-identical to the
+ * CPU checker's copy). router_bias: [E] host array or NULL. */
+QeMoe *qe_moe_create_synthetic(const QeMoeConfig *cfg, uint64_t seed, uint32_t block, const float *router_bias);
+
+void qe_moe_free(QeMoe *m);
+
+/* out[T][hidden] = moe(x[T][hidden]) for T >= 1 independent tokens, host buffers (x, out may not alias).
+ * Replaces T calls of moe_layer_step (engine/src/moe_layer.c:66-89). 0 ok, -1 error (out untouched). */
+int qe_moe_forward(QeMoe *m, int T, const float *x, float *out);
+
+/* Same on device buffers of m's device, enqueued on `stream` (a cudaStream_t, NULL = legacy default),
+ * no host synchronisation. */
+int qe_moe_forward_device(QeMoe *m, int T, const float *x, float *out, void *stream);
+
+/* Routing only (moe_layer.c:29-37): idx[T][top_k] expert ids, score[T][top_k] renormalised weights,
+ * host buffers. */
+int qe_moe_route(QeMoe *m, int T, const float *x, int32_t *idx, float *score);
+
+/* Block accessors. */
+int qe_moe_hidden(const QeMoe *m);
+int qe_moe_top_k(const QeMoe *m);
+size_t qe_moe_weight_bytes(const QeMoe *m);   /* HBM bytes held by this block's weights */
+
+/* ---- kernel-level entry points (host buffers), the GPU counterparts of the reference's ops ---- */
+
+/* y[rows] = W x, W one MLX-affine QMat (engine/include/qmat.h:32, engine/src/qmat.c:15-49). Same validation
+ * as qmat_matvec: bits in {4,8}, group_size in {32,64,128}, rows > 0, cols > 0 and a multiple of
+ * group_size, cols/group_size <= 4096; on error returns -1 and leaves y untouched. */
+int qe_qmat_matvec(const uint32_t *w, const uint16_t *scales, const uint16_t *biases, int rows, int cols, int bits,
+                   int group_size, const float *x, float *y);
+
+/* T softmax + top-k + renormalisations on given logits[T][E] (engine/src/ops.c:29-73, moe_layer.c:31-36).
+ * probs[T][E] (may be NULL), idx[T][k], score[T][k]. 1 <= k <= min(16, E), E <= 512. */
+int qe_route_logits(int T, int E, int k, const float *logits, float *probs, int32_t *idx, float *score);
+
+/* Element-wise ops of engine/src/ops.c:16-27 on the GPU (host buffers, n >= 1). */
+int qe_op_silu_mul(float *out, const float *gate, const float *up, int n);
+int qe_op_sigmoid(float *out, const float *x, int n);
+/* The device expf used by softmax, on n inputs (for comparison with the host C library's expf). */
+int qe_op_expf(float *out, const float *x, int n);
+
+/* ---- engine-level statistics (engine/include/qengine.h:20-23 counterparts) ---- */
+double qe_expert_gb_read(void);        /* GB of expert weights streamed from HBM by qe_moe_forward */
+double qe_expert_read_seconds(void);   /* GPU seconds spent in qe_moe_forward's kernels            */
+int qe_device_count(void);
+
+/* ---- profiling (no reference counterpart: the reference times only its expert reads, moe_layer.c:74-78) ---- */
+enum { QE_STAGE_ROUTER = 0, QE_STAGE_TOPK, QE_STAGE_BUCKET, QE_STAGE_GATEUP, QE_STAGE_DOWN, QE_STAGE_COMBINE,
+       QE_STAGES };
+/* Record CUDA events around every stage of every forward pass on `device` from now on. */
+int qe_profile_begin(int device);
+/* Stop recording; stage_ms[QE_STAGES] = summed GPU milliseconds per stage, *passes = passes recorded. */
+int qe_profile_end(int device, double *stage_ms, int *passes);
+/* Kernels launched by this library since process start. */
+unsigned long long qe_kernel_launches(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,133 @@
+/* bucket.cu: token bucketing for the expert kernels.
+ *
+ * Replaces the reference's per-token expert loop (engine/src/moe_layer.c:79-83, prefill = T calls) and
+ * the batched template of its MLX path (engine/hybrid/hybrid.py:177-189: unique experts + inverse index,
+ * tokens sorted by expert) with a histogram + prefix scan + scatter on the GPU. Every (token, slot) pair
+ * p = t*(k+1) + j (j = k is the shared expert) lands in its expert's bucket; the active buckets and the
+ * work items of the gate/up and down kernels are listed so those kernels run a compact grid.
+ * Numerics do not depend on the order of pairs inside a bucket (every pair is an independent MMA column).
+ */
+#include "qe_common.cuh"
+#include "qe_kernels.h"
+
+namespace {
+
+constexpr int kThreads = 1024;
+
+/* Exclusive scan of n ints in place by one warp (n <= a few thousand). Returns the total. */
+__device__ int warp_exclusive_scan(int *a, int n, int lane) {
+    const int per = (n + 31) / 32;
+    const int b0 = lane * per, b1 = min(n, b0 + per);
+    int local = 0;
+    for (int i = b0; i < b1; i++) local += a[i];
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(QE_FULL, incl, o);
+        if (lane >= o) incl += v;
+    }
+    int run = incl - local;
+    for (int i = b0; i < b1; i++) {
+        const int v = a[i];
+        a[i] = run;
+        run += v;
+    }
+    return __shfl_sync(QE_FULL, incl, 31);
+}
+
+__global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restrict__ idx, int T, int E, int k,
+                                                          int tiles_gu, int tiles_sh_gu, int tiles_dn, int chunk,
+                                                          QeBuckets b) {
+    extern __shared__ int sm[];
+    int *cnt = sm;                 /* [E+1] */
+    int *off = cnt + (E + 1);      /* [E+2] */
+    int *cur = off + (E + 2);      /* [E+1] */
+    int *flag = cur + (E + 1);     /* [E+2] active-slot scan */
+    int *igu = flag + (E + 2);     /* [E+2] */
+    int *idn = igu + (E + 2);      /* [E+2] */
+    const int tid = threadIdx.x, lane = tid & 31;
+    for (int e = tid; e <= E; e += kThreads) cnt[e] = 0;
+    __syncthreads();
+    const int npairs = T * k;
+    for (int q = tid; q < npairs; q += kThreads) {
+        const int e = idx[q];
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (tid == 0) cnt[E] = T;
+    __syncthreads();
+    for (int e = tid; e <= E; e += kThreads) {
+        off[e] = cnt[e];
+        const int active = cnt[e] > 0;
+        flag[e] = active;
+        const int chunks = (cnt[e] + chunk - 1) / chunk;
+        igu[e] = chunks * (e == E ? tiles_sh_gu : tiles_gu);
+        idn[e] = chunks * tiles_dn;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        const int total = warp_exclusive_scan(off, E + 1, lane);
+        if (lane == 0) off[E + 1] = total;
+    } else if (tid < 64) {
+        const int na = warp_exclusive_scan(flag, E + 1, lane);
+        if (lane == 0) flag[E + 1] = na;
+    }
+    __syncthreads();
+    /* compact the per-slot item counts into active-slot order, then scan them */
+    for (int e = tid; e <= E; e += kThreads) {
+        cur[e] = off[e];
+        if (cnt[e] > 0) {
+            const int a = flag[e];
+            b.slot_expert[a] = e;
+        }
+    }
+    __syncthreads();
+    const int na = flag[E + 1];
+    /* reuse the tail of idn/igu as compact arrays: build compact lists in registers via the slot map */
+    for (int a = tid; a < na; a += kThreads) {
+        const int e = b.slot_expert[a];
+        b.slot_items[a] = igu[e];
+        b.slot_items[(E + 2) + a] = idn[e];
+    }
+    __syncthreads();
+    __threadfence_block();
+    if (tid == 0) {
+        int sg = 0, sd = 0;
+        for (int a = 0; a < na; a++) {
+            const int vg = b.slot_items[a], vd = b.slot_items[(E + 2) + a];
+            b.slot_items[a] = sg;
+            b.slot_items[(E + 2) + a] = sd;
+            sg += vg;
+            sd += vd;
+        }
+        b.slot_items[na] = sg;
+        b.slot_items[(E + 2) + na] = sd;
+        b.n_active[0] = na;
+        b.n_active[1] = sg;
+        b.n_active[2] = sd;
+    }
+    /* scatter the pairs into their buckets */
+    for (int q = tid; q < npairs; q += kThreads) {
+        const int e = idx[q];
+        if (e < 0 || e >= E) continue;
+        const int t = q / k, j = q % k;
+        const int pos = atomicAdd(&cur[e], 1);
+        b.pairs[pos] = t * (k + 1) + j;
+    }
+    for (int t = tid; t < T; t += kThreads) b.pairs[off[E] + t] = t * (k + 1) + k;
+    for (int e = tid; e <= E; e += kThreads) {
+        b.counts[e] = cnt[e];
+        b.offsets[e] = off[e];
+    }
+    if (tid == 0) b.offsets[E + 1] = off[E + 1];
+}
+
+}  // namespace
+
+int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int tiles_gu, int tiles_sh_gu, int tiles_dn,
+                     int chunk, const QeBuckets *b, cudaStream_t s) {
+    const size_t smem = sizeof(int) * (size_t)(6 * (E + 2));
+    bucket_kernel<<<1, kThreads, smem, s>>>(idx, T, E, k, tiles_gu, tiles_sh_gu, tiles_dn, chunk, *b);
+    QE_CHECK(cudaGetLastError());
+    return 0;
+}

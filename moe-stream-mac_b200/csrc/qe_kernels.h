@@ -1,0 +1,63 @@
+/* qe_kernels.h: internal launchers shared by the .cu files of libqengine_b200 (not part of the C ABI). */
+#ifndef QE_KERNELS_H
+#define QE_KERNELS_H
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+/* One quantized matrix in the MLX affine layout (engine/include/qmat.h:3-11), resident in HBM.
+ * For routed experts the pointers cover all E experts: expert e starts at w + e*rows*wpr words and at
+ * scales/biases + e*rows*ngroups halves (engine/src/loader.c:35-41). */
+struct QeQDev {
+    const uint32_t *w;
+    const uint16_t *scales;
+    const uint16_t *biases;
+    int rows, cols, bits, group_size;
+};
+
+/* Routing: fp32 router logits for E experts plus one extra column (index E) holding the shared-expert
+ * gate logit, logits[T][E+1]. */
+int qe_launch_router_f32(const float *W /*[E+1][H]*/, const float *bias /*[E] or null*/, const float *x,
+                         int T, int H, int E, float *logits, cudaStream_t s);
+int qe_launch_router_qmat(const QeQDev *router /*[E][H]*/, const QeQDev *sh_router /*[1][H]*/, const float *x,
+                          int T, int H, int E, float *logits, cudaStream_t s);
+int qe_launch_route_topk(const float *logits, int ld, int T, int E, int k, int32_t *idx, float *score,
+                         float *probs /* [T][E] or null */, cudaStream_t s);
+
+/* Bucketing: expert-sorted (token, slot) pairs and the work lists of the expert kernels. */
+struct QeBuckets {
+    int32_t *counts;      /* [E+1]                                            */
+    int32_t *offsets;     /* [E+2]                                            */
+    int32_t *cursor;      /* [E+1]                                            */
+    int32_t *pairs;       /* [T*(k+1)] pair ids p = t*(k+1)+j, sorted by slot */
+    int32_t *slot_expert; /* [E+1] active slots -> expert id (E = shared)     */
+    int32_t *slot_items;  /* [2][E+2] per-slot work-item prefix, gate/up & down */
+    int32_t *n_active;    /* [3]: active slots, gate/up items, down items     */
+};
+int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int tiles_gu, int tiles_sh_gu, int tiles_dn,
+                     int chunk, const QeBuckets *b, cudaStream_t s);
+
+/* Expert kernels (mma.sync split-bf16 path). */
+struct QeExpertArgs {
+    QeQDev gate, up, down;            /* routed experts, [E][...]           */
+    QeQDev sh_gate, sh_up, sh_down;   /* shared expert                      */
+    int E, k, hidden, inter, sh_inter;
+};
+int qe_launch_gateup(const QeExpertArgs *a, const float *x, const QeBuckets *b, int T, float *h3 /*[T*(k+1)][I]*/,
+                     int ldh, int grid, cudaStream_t s);
+int qe_launch_down(const QeExpertArgs *a, const float *h3, int ldh, const QeBuckets *b, int T,
+                   float *ybuf /*[T*(k+1)][H]*/, int grid, cudaStream_t s);
+int qe_launch_combine(const float *ybuf, const float *score, const float *logits, int ld_logits, int T, int E,
+                      int k, int H, float *out, cudaStream_t s);
+
+/* Generic quantized matrix-vector products (engine/src/qmat.c:15-49 semantics) over T vectors. */
+int qe_launch_qmatvec(const QeQDev *m, const float *x, int T, float *y, cudaStream_t s);
+
+/* Synthetic weights generated in HBM (csrc/synth.h). */
+int qe_launch_synth_qmat(uint64_t seed, uint32_t block, uint32_t stream, int n, int rows, int cols, int bits,
+                         int gs, uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s);
+int qe_launch_synth_normal(uint64_t seed, uint32_t block, uint32_t stream, size_t n, float sigma_c, float *out,
+                           cudaStream_t s);
+
+int qe_num_sms(void);
+
+#endif

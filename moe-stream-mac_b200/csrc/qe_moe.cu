@@ -1,0 +1,659 @@
+/* qe_moe.cu: the C ABI of libqengine_b200 (include/qe_moe.h) and the block pipeline.
+ *
+ * Pipeline of one forward (replacing moe_layer_step, engine/src/moe_layer.c:66-89, for T tokens at once):
+ *   1. router logits [T][E+1] (column E = shared-expert gate logit)          route.cu
+ *   2. softmax + top-k + renormalise -> idx[T][k], score[T][k]                route.cu
+ *   3. bucket (token, slot) pairs by expert, list the active experts         bucket.cu
+ *   4. gate/up projections + SwiGLU for every (pair, expert) -> h3           expert_mma.cu
+ *   5. down projection -> y per pair                                         expert_mma.cu
+ *   6. out = sum_i score_i * y_i + sigmoid(gate logit) * y_shared           expert_mma.cu
+ * The expert weights are resident in HBM for the handle's lifetime (the reference preads them from SSD
+ * per token: engine/src/expert_store.c:54-61, moe_layer.c:42-55).
+ */
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+#include <atomic>
+#include <mutex>
+#include <vector>
+
+#include "qe_common.cuh"
+#include "qe_kernels.h"
+#include "synth.h"
+#include "../../include/qe_moe.h"
+
+int qe_expert_rows_per_cta(void);
+
+/* ------------------------------------------------------------------ per-device context and workspace */
+
+namespace {
+
+struct DevCtx {
+    bool init = false;
+    cudaStream_t stream = nullptr;
+    int sms = 0;
+    void *ws = nullptr;       /* scratch workspace shared by all handles on this device */
+    size_t ws_bytes = 0;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+};
+
+std::mutex g_mu;
+DevCtx g_dev[64];
+std::atomic<unsigned long long> g_bytes_read{0};
+double g_gpu_seconds = 0.0;
+std::atomic<unsigned long long> g_launches{0};
+
+/* Stage profiling: when enabled, every pass records one event before the router and one after each of
+ * the QE_STAGES stages on the stream it runs on; qe_profile_end sums the per-stage elapsed times. */
+constexpr int kStages = 6;
+struct Prof {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+};
+Prof g_prof[64];
+
+cudaEvent_t prof_event(int dev) {
+    Prof &p = g_prof[dev];
+    if (p.used == p.pool.size()) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+        p.pool.push_back(e);
+    }
+    return p.pool[p.used++];
+}
+
+void prof_mark(int dev, cudaStream_t s) {
+    if (!g_prof[dev].on) return;
+    cudaEvent_t e = prof_event(dev);
+    if (e) cudaEventRecord(e, s);
+}
+
+int dev_ctx(int device, DevCtx **out) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) QE_FAIL("no CUDA device available");
+    if (device < 0 || device >= n || device >= 64) QE_FAIL("device %d out of range (%d devices)", device, n);
+    QE_CHECK(cudaSetDevice(device));
+    DevCtx &d = g_dev[device];
+    if (!d.init) {
+        int major = 0;
+        QE_CHECK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+        if (major != 10) QE_FAIL("device %d has compute capability %d.x; this library is built for sm_100a", device, major);
+        QE_CHECK(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, device));
+        QE_CHECK(cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking));
+        QE_CHECK(cudaEventCreate(&d.ev0));
+        QE_CHECK(cudaEventCreate(&d.ev1));
+        d.init = true;
+    }
+    *out = &d;
+    return 0;
+}
+
+int ensure_ws(DevCtx *d, size_t bytes) {
+    if (d->ws_bytes >= bytes) return 0;
+    if (d->ws) {
+        QE_CHECK(cudaStreamSynchronize(d->stream));
+        QE_CHECK(cudaDeviceSynchronize());
+        cudaFree(d->ws);
+        d->ws = nullptr;
+        d->ws_bytes = 0;
+    }
+    QE_CHECK(cudaMalloc(&d->ws, bytes));
+    d->ws_bytes = bytes;
+    return 0;
+}
+
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+/* Carves a workspace into the per-forward buffers. */
+struct Scratch {
+    float *x, *out, *logits, *score, *h3, *ybuf;
+    int32_t *idx;
+    QeBuckets b;
+};
+
+size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
+    const int E = c.E, k = c.top_k, I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> char * {
+        char *p = base ? base + off : nullptr;
+        off += align256(bytes);
+        return p;
+    };
+    const size_t npair = (size_t)T * (k + 1);
+    Scratch t;
+    t.x = (float *)take(sizeof(float) * (size_t)T * c.hidden);
+    t.out = (float *)take(sizeof(float) * (size_t)T * c.hidden);
+    t.logits = (float *)take(sizeof(float) * (size_t)T * (E + 1));
+    t.score = (float *)take(sizeof(float) * (size_t)T * k);
+    t.idx = (int32_t *)take(sizeof(int32_t) * (size_t)T * k);
+    t.h3 = (float *)take(sizeof(float) * npair * I);
+    t.ybuf = (float *)take(sizeof(float) * npair * c.hidden);
+    t.b.counts = (int32_t *)take(sizeof(int32_t) * (E + 1));
+    t.b.offsets = (int32_t *)take(sizeof(int32_t) * (E + 2));
+    t.b.cursor = (int32_t *)take(sizeof(int32_t) * (E + 1));
+    t.b.pairs = (int32_t *)take(sizeof(int32_t) * npair);
+    t.b.slot_expert = (int32_t *)take(sizeof(int32_t) * (E + 2));
+    t.b.slot_items = (int32_t *)take(sizeof(int32_t) * 2 * (E + 2));
+    t.b.n_active = (int32_t *)take(sizeof(int32_t) * 4);
+    if (s) *s = t;
+    return off;
+}
+
+}  // namespace
+
+/* ------------------------------------------------------------------ handle */
+
+struct QeMoe {
+    QeMoeConfig cfg;
+    int device;
+    void *weights;          /* one HBM allocation holding every tensor of the block */
+    size_t weight_bytes;
+    float *router_w;        /* [E+1][H] (F32 mode; row E = shared gate) */
+    float *router_bias;     /* [E] or null */
+    QeQDev router_q, sh_router_q;
+    QeExpertArgs ex;
+    size_t expert_bytes;    /* bytes of one routed expert (gate+up+down codes, scales, biases) */
+};
+
+namespace {
+
+int validate(const QeMoeConfig *c) {
+    if (!c) QE_FAIL("null config");
+    if (c->top_k < 1 || c->top_k > 16) QE_FAIL("top_k=%d outside [1, 16] (MOE_MAX_TOPK)", c->top_k);
+    if (c->E < c->top_k || c->E > 512) QE_FAIL("E=%d outside [top_k, 512]", c->E);
+    if (c->bits != 4 && c->bits != 8) QE_FAIL("bits=%d: only 4 and 8 are supported", c->bits);
+    if (c->group_size != 32 && c->group_size != 64 && c->group_size != 128)
+        QE_FAIL("group_size=%d: only 32, 64 and 128 are supported", c->group_size);
+    if (c->hidden <= 0 || c->inter <= 0 || c->sh_inter <= 0) QE_FAIL("non-positive dimension");
+    if (c->hidden % c->group_size || c->inter % c->group_size || c->sh_inter % c->group_size)
+        QE_FAIL("hidden/inter/sh_inter must be multiples of group_size %d", c->group_size);
+    if (c->hidden > 8192) QE_FAIL("hidden=%d > 8192", c->hidden);
+    if (c->router_mode != QE_ROUTER_F32 && c->router_mode != QE_ROUTER_QMAT) QE_FAIL("bad router_mode");
+    if (c->router_mode == QE_ROUTER_QMAT && c->router_bits != 4 && c->router_bits != 8)
+        QE_FAIL("router_bits=%d: only 4 and 8", c->router_bits);
+    return 0;
+}
+
+size_t qbytes(int n, int rows, int cols, int bits, int gs, size_t *wb, size_t *gb) {
+    *wb = (size_t)n * rows * ((size_t)cols * bits / 32) * 4;
+    *gb = (size_t)n * rows * ((size_t)cols / gs) * 2;
+    return *wb + 2 * *gb;
+}
+
+/* Allocate the handle and carve its HBM block. */
+QeMoe *alloc_handle(const QeMoeConfig *c) {
+    if (validate(c)) return nullptr;
+    DevCtx *d;
+    if (dev_ctx(c->device, &d)) return nullptr;
+    QeMoe *m = (QeMoe *)calloc(1, sizeof(QeMoe));
+    if (!m) return nullptr;
+    m->cfg = *c;
+    if (m->cfg.max_tokens < 1) m->cfg.max_tokens = 4096;
+    m->device = c->device;
+    const int E = c->E, H = c->hidden, I = c->inter, Is = c->sh_inter, b = c->bits, gs = c->group_size;
+    struct Part { int n, rows, cols, bits; QeQDev *dst; };
+    Part parts[8] = {
+        {E, I, H, b, &m->ex.gate}, {E, I, H, b, &m->ex.up}, {E, H, I, b, &m->ex.down},
+        {1, Is, H, b, &m->ex.sh_gate}, {1, Is, H, b, &m->ex.sh_up}, {1, H, Is, b, &m->ex.sh_down},
+        {c->router_mode == QE_ROUTER_QMAT ? 1 : 0, E, H, c->router_bits, &m->router_q},
+        {c->router_mode == QE_ROUTER_QMAT ? 1 : 0, 1, H, c->router_bits, &m->sh_router_q}};
+    size_t total = 0;
+    for (auto &p : parts) {
+        if (!p.n) continue;
+        size_t wb, gb;
+        qbytes(p.n, p.rows, p.cols, p.bits, gs, &wb, &gb);
+        total += align256(wb) + 2 * align256(gb);
+    }
+    if (c->router_mode == QE_ROUTER_F32) total += align256(sizeof(float) * (size_t)(E + 1) * H) + align256(4 * (size_t)E);
+    char *base = nullptr;
+    if (cudaMalloc((void **)&base, total) != cudaSuccess) {
+        fprintf(stderr, "qengine_b200: cannot allocate %zu bytes of HBM for the block\n", total);
+        free(m);
+        return nullptr;
+    }
+    m->weights = base;
+    m->weight_bytes = total;
+    size_t off = 0;
+    for (auto &p : parts) {
+        if (!p.n) continue;
+        size_t wb, gb;
+        qbytes(p.n, p.rows, p.cols, p.bits, gs, &wb, &gb);
+        p.dst->w = (const uint32_t *)(base + off); off += align256(wb);
+        p.dst->scales = (const uint16_t *)(base + off); off += align256(gb);
+        p.dst->biases = (const uint16_t *)(base + off); off += align256(gb);
+        p.dst->rows = p.rows; p.dst->cols = p.cols; p.dst->bits = p.bits; p.dst->group_size = gs;
+    }
+    if (c->router_mode == QE_ROUTER_F32) {
+        m->router_w = (float *)(base + off); off += align256(sizeof(float) * (size_t)(E + 1) * H);
+        m->router_bias = (float *)(base + off); off += align256(4 * (size_t)E);
+    }
+    m->ex.E = E; m->ex.k = c->top_k; m->ex.hidden = H; m->ex.inter = I; m->ex.sh_inter = Is;
+    size_t wb, gb;
+    m->expert_bytes = qbytes(1, I, H, b, gs, &wb, &gb) * 2 + qbytes(1, H, I, b, gs, &wb, &gb);
+    return m;
+}
+
+int upload_q(const QeQDev *dst, const QeQTensor *src, int n, cudaStream_t s) {
+    if (!src->w || !src->scales || !src->biases) QE_FAIL("missing quantized tensor");
+    const size_t wb = (size_t)n * dst->rows * ((size_t)dst->cols * dst->bits / 32) * 4;
+    const size_t gb = (size_t)n * dst->rows * ((size_t)dst->cols / dst->group_size) * 2;
+    QE_CHECK(cudaMemcpyAsync((void *)dst->w, src->w, wb, cudaMemcpyHostToDevice, s));
+    QE_CHECK(cudaMemcpyAsync((void *)dst->scales, src->scales, gb, cudaMemcpyHostToDevice, s));
+    QE_CHECK(cudaMemcpyAsync((void *)dst->biases, src->biases, gb, cudaMemcpyHostToDevice, s));
+    return 0;
+}
+
+__global__ void synth_qmat_kernel(uint64_t seed, uint32_t block, uint32_t stream, size_t nwords, size_t ngroups,
+                                  float scale_c, float neg_half, uint32_t *w, uint16_t *sc, uint16_t *bi) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nwords; i += stride)
+        w[i] = syn_code_word(seed, block, stream, i);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < ngroups; i += stride) {
+        uint16_t s, b;
+        syn_scale_bias(seed, block, stream, i, scale_c, neg_half, &s, &b);
+        sc[i] = s;
+        bi[i] = b;
+    }
+}
+
+__global__ void synth_normal_kernel(uint64_t seed, uint32_t block, uint32_t stream, size_t n, float sigma_c,
+                                    float *out) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = syn_normal(syn_hash(seed, block, stream, i), sigma_c);
+}
+
+__global__ void ops_kernel(int op, const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ out,
+                           int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    if (op == 0) out[i] = qe_silu_mul(a[i], b[i]);
+    else if (op == 1) out[i] = qe_sigmoid(a[i]);
+    else out[i] = qe_expf(a[i]);
+}
+
+}  // namespace
+
+int qe_launch_synth_qmat(uint64_t seed, uint32_t block, uint32_t stream, int n, int rows, int cols, int bits, int gs,
+                         uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s) {
+    const size_t nwords = (size_t)n * rows * ((size_t)cols * bits / 32), ngroups = (size_t)n * rows * (cols / gs);
+    synth_qmat_kernel<<<1184, 256, 0, s>>>(seed, block, stream, nwords, ngroups, syn_scale_c(bits),
+                                           syn_neg_half_range(bits), w, sc, bi);
+    QE_CHECK(cudaGetLastError());
+    return 0;
+}
+
+int qe_launch_synth_normal(uint64_t seed, uint32_t block, uint32_t stream, size_t n, float sigma_c, float *out,
+                           cudaStream_t s) {
+    synth_normal_kernel<<<592, 256, 0, s>>>(seed, block, stream, n, sigma_c, out);
+    QE_CHECK(cudaGetLastError());
+    return 0;
+}
+
+int qe_num_sms(void) {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+extern "C" {
+
+QeMoe *qe_moe_create(const QeMoeConfig *cfg, const QeMoeWeights *w) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!w) { fprintf(stderr, "qengine_b200: null weights\n"); return nullptr; }
+    QeMoe *m = alloc_handle(cfg);
+    if (!m) return nullptr;
+    DevCtx *d = &g_dev[m->device];
+    cudaStream_t s = d->stream;
+    int rc = upload_q(&m->ex.gate, &w->gate, cfg->E, s) || upload_q(&m->ex.up, &w->up, cfg->E, s) ||
+             upload_q(&m->ex.down, &w->down, cfg->E, s) || upload_q(&m->ex.sh_gate, &w->sh_gate, 1, s) ||
+             upload_q(&m->ex.sh_up, &w->sh_up, 1, s) || upload_q(&m->ex.sh_down, &w->sh_down, 1, s);
+    if (!rc && cfg->router_mode == QE_ROUTER_QMAT)
+        rc = upload_q(&m->router_q, &w->router_q, 1, s) || upload_q(&m->sh_router_q, &w->sh_router_q, 1, s);
+    if (!rc && cfg->router_mode == QE_ROUTER_F32) {
+        if (!w->router_f32 || !w->sh_gate_f32) {
+            fprintf(stderr, "qengine_b200: fp32 router mode needs router_f32 and sh_gate_f32\n");
+            rc = -1;
+        } else {
+            const size_t H = cfg->hidden, E = cfg->E;
+            rc = cudaMemcpyAsync(m->router_w, w->router_f32, 4 * E * H, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+                 cudaMemcpyAsync(m->router_w + E * H, w->sh_gate_f32, 4 * H, cudaMemcpyHostToDevice, s) != cudaSuccess;
+            if (!rc && w->router_bias)
+                rc = cudaMemcpyAsync(m->router_bias, w->router_bias, 4 * E, cudaMemcpyHostToDevice, s) != cudaSuccess;
+            if (!w->router_bias) m->router_bias = nullptr;
+        }
+    }
+    if (!rc) rc = cudaStreamSynchronize(s) != cudaSuccess;
+    if (rc) {
+        fprintf(stderr, "qengine_b200: weight upload failed\n");
+        cudaFree(m->weights);
+        free(m);
+        return nullptr;
+    }
+    return m;
+}
+
+QeMoe *qe_moe_create_synthetic(const QeMoeConfig *cfg, uint64_t seed, uint32_t block, const float *router_bias) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    QeMoe *m = alloc_handle(cfg);
+    if (!m) return nullptr;
+    cudaStream_t s = g_dev[m->device].stream;
+    const int E = cfg->E, H = cfg->hidden, I = cfg->inter, Is = cfg->sh_inter, b = cfg->bits, gs = cfg->group_size;
+    auto gen = [&](const QeQDev &q, uint32_t stream, int n) {
+        return qe_launch_synth_qmat(seed, block, stream, n, q.rows, q.cols, q.bits, gs, (uint32_t *)q.w,
+                                    (uint16_t *)q.scales, (uint16_t *)q.biases, s);
+    };
+    int rc = gen(m->ex.gate, SYN_GATE, E) || gen(m->ex.up, SYN_UP, E) || gen(m->ex.down, SYN_DOWN, E) ||
+             gen(m->ex.sh_gate, SYN_SH_GATE, 1) || gen(m->ex.sh_up, SYN_SH_UP, 1) || gen(m->ex.sh_down, SYN_SH_DOWN, 1);
+    (void)I; (void)Is; (void)b;
+    if (!rc && cfg->router_mode == QE_ROUTER_QMAT)
+        rc = gen(m->router_q, SYN_ROUTER, 1) || gen(m->sh_router_q, SYN_SHGATE, 1);
+    if (!rc && cfg->router_mode == QE_ROUTER_F32) {
+        const float c = syn_sigma_c(0.02);
+        rc = qe_launch_synth_normal(seed, block, SYN_ROUTER, (size_t)E * H, c, m->router_w, s) ||
+             qe_launch_synth_normal(seed, block, SYN_SHGATE, (size_t)H, c, m->router_w + (size_t)E * H, s);
+        if (!rc && router_bias)
+            rc = cudaMemcpyAsync(m->router_bias, router_bias, 4 * (size_t)E, cudaMemcpyHostToDevice, s) != cudaSuccess;
+        if (!router_bias) m->router_bias = nullptr;
+    }
+    if (!rc) rc = cudaStreamSynchronize(s) != cudaSuccess;
+    if (rc) {
+        fprintf(stderr, "qengine_b200: synthetic block generation failed\n");
+        cudaFree(m->weights);
+        free(m);
+        return nullptr;
+    }
+    return m;
+}
+
+void qe_moe_free(QeMoe *m) {
+    if (!m) return;
+    std::lock_guard<std::mutex> lock(g_mu);
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(g_dev[m->device].stream);
+    cudaFree(m->weights);
+    free(m);
+}
+
+int qe_moe_hidden(const QeMoe *m) { return m ? m->cfg.hidden : -1; }
+int qe_moe_top_k(const QeMoe *m) { return m ? m->cfg.top_k : -1; }
+size_t qe_moe_weight_bytes(const QeMoe *m) { return m ? m->weight_bytes : 0; }
+
+}  // extern "C"
+
+namespace {
+
+/* Routing for one pass of T tokens: logits + idx/score in the scratch. */
+int run_route(QeMoe *m, const float *x, int T, Scratch &sc, cudaStream_t s) {
+    const QeMoeConfig &c = m->cfg;
+    if (c.router_mode == QE_ROUTER_F32) {
+        if (qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, s)) return -1;
+    } else {
+        if (qe_launch_router_qmat(&m->router_q, &m->sh_router_q, x, T, c.hidden, c.E, sc.logits, s)) return -1;
+    }
+    return qe_launch_route_topk(sc.logits, c.E + 1, T, c.E, c.top_k, sc.idx, sc.score, nullptr, s);
+}
+
+int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, cudaStream_t s) {
+    const QeMoeConfig &c = m->cfg;
+    const int dev = m->device;
+    prof_mark(dev, s);
+    if (c.router_mode == QE_ROUTER_F32) {
+        if (qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, s)) return -1;
+        g_launches += 1;
+    } else {
+        if (qe_launch_router_qmat(&m->router_q, &m->sh_router_q, x, T, c.hidden, c.E, sc.logits, s)) return -1;
+        g_launches += 2;
+    }
+    prof_mark(dev, s);
+    if (qe_launch_route_topk(sc.logits, c.E + 1, T, c.E, c.top_k, sc.idx, sc.score, nullptr, s)) return -1;
+    g_launches += 1;
+    prof_mark(dev, s);
+    const int R = qe_expert_rows_per_cta();
+    const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R, tiles_dn = (c.hidden + R - 1) / R;
+    const int chunk = T < 8 ? T : 8;
+    if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, tiles_gu, tiles_sh, tiles_dn, chunk, &sc.b, s)) return -1;
+    prof_mark(dev, s);
+    /* grid: enough CTAs for every item in the common case, grid-stride beyond */
+    const long long slots = std::min<long long>((long long)c.E, (long long)T * c.top_k) + 1;
+    const long long chunks = ((long long)T * (c.top_k + 1) + chunk - 1) / chunk + slots;
+    const int tmax = std::max(tiles_gu, tiles_sh);
+    const int grid_gu = (int)std::min<long long>(chunks * tmax, 16LL * sms);
+    const int grid_dn = (int)std::min<long long>(chunks * tiles_dn, 16LL * sms);
+    const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
+    if (qe_launch_gateup(&m->ex, x, &sc.b, T, sc.h3, I, grid_gu, s)) return -1;
+    prof_mark(dev, s);
+    if (qe_launch_down(&m->ex, sc.h3, I, &sc.b, T, sc.ybuf, grid_dn, s)) return -1;
+    prof_mark(dev, s);
+    if (qe_launch_combine(sc.ybuf, sc.score, sc.logits, c.E + 1, T, c.E, c.top_k, c.hidden, out, s)) return -1;
+    prof_mark(dev, s);
+    g_launches += 4;
+    return 0;
+}
+
+void trace_route(const QeMoe *m, const int32_t *idx, int T) {
+    /* QE_TRACE=<file>: append int32 layer, idx[top_k] per token (engine/src/moe_layer.c:57-64) */
+    static FILE *f;
+    static int checked;
+    if (!checked) {
+        const char *p = getenv("QE_TRACE");
+        f = p ? fopen(p, "ab") : nullptr;
+        checked = 1;
+    }
+    if (!f) return;
+    const int32_t layer = m->cfg.layer;
+    for (int t = 0; t < T; t++) {
+        fwrite(&layer, 4, 1, f);
+        fwrite(idx + (size_t)t * m->cfg.top_k, 4, (size_t)m->cfg.top_k, f);
+    }
+    fflush(f);
+}
+
+}  // namespace
+
+extern "C" {
+
+int qe_moe_forward_device(QeMoe *m, int T, const float *x, float *out, void *stream) {
+    if (!m || !x || !out || T < 1) QE_FAIL("forward: bad arguments");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int P = std::min(T, m->cfg.max_tokens);
+    if (ensure_ws(d, scratch_layout(m->cfg, P, nullptr, nullptr))) return -1;
+    Scratch sc;
+    scratch_layout(m->cfg, P, (char *)d->ws, &sc);
+    for (int t0 = 0; t0 < T; t0 += P) {
+        const int n = std::min(P, T - t0);
+        const size_t o = (size_t)t0 * m->cfg.hidden;
+        if (run_pass(m, x + o, out + o, n, sc, d->sms, s)) return -1;
+    }
+    return 0;
+}
+
+int qe_moe_forward(QeMoe *m, int T, const float *x, float *out) {
+    if (!m || !x || !out || T < 1) QE_FAIL("forward: bad arguments");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = d->stream;
+    const int P = std::min(T, m->cfg.max_tokens);
+    if (ensure_ws(d, scratch_layout(m->cfg, P, nullptr, nullptr))) return -1;
+    Scratch sc;
+    scratch_layout(m->cfg, P, (char *)d->ws, &sc);
+    const size_t H = m->cfg.hidden;
+    const bool tracing = getenv("QE_TRACE") != nullptr;
+    std::vector<int32_t> idx_host;
+    unsigned long long experts_touched = 0;
+    QE_CHECK(cudaEventRecord(d->ev0, s));
+    for (int t0 = 0; t0 < T; t0 += P) {
+        const int n = std::min(P, T - t0);
+        QE_CHECK(cudaMemcpyAsync(sc.x, x + (size_t)t0 * H, sizeof(float) * n * H, cudaMemcpyHostToDevice, s));
+        if (run_pass(m, sc.x, sc.out, n, sc, d->sms, s)) return -1;
+        QE_CHECK(cudaMemcpyAsync(out + (size_t)t0 * H, sc.out, sizeof(float) * n * H, cudaMemcpyDeviceToHost, s));
+        int32_t na = 0;
+        QE_CHECK(cudaMemcpyAsync(&na, sc.b.n_active, 4, cudaMemcpyDeviceToHost, s));
+        if (tracing) {
+            idx_host.resize((size_t)n * m->cfg.top_k);
+            QE_CHECK(cudaMemcpyAsync(idx_host.data(), sc.idx, 4 * idx_host.size(), cudaMemcpyDeviceToHost, s));
+        }
+        QE_CHECK(cudaStreamSynchronize(s));
+        experts_touched += (unsigned long long)(na > 0 ? na - 1 : 0);
+        if (tracing) trace_route(m, idx_host.data(), n);
+    }
+    QE_CHECK(cudaEventRecord(d->ev1, s));
+    QE_CHECK(cudaEventSynchronize(d->ev1));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, d->ev0, d->ev1);
+    g_gpu_seconds += ms * 1e-3;
+    g_bytes_read += experts_touched * (unsigned long long)m->expert_bytes;
+    return 0;
+}
+
+int qe_moe_route(QeMoe *m, int T, const float *x, int32_t *idx, float *score) {
+    if (!m || !x || !idx || !score || T < 1) QE_FAIL("route: bad arguments");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = d->stream;
+    const int P = std::min(T, m->cfg.max_tokens);
+    if (ensure_ws(d, scratch_layout(m->cfg, P, nullptr, nullptr))) return -1;
+    Scratch sc;
+    scratch_layout(m->cfg, P, (char *)d->ws, &sc);
+    const size_t H = m->cfg.hidden, k = m->cfg.top_k;
+    for (int t0 = 0; t0 < T; t0 += P) {
+        const int n = std::min(P, T - t0);
+        QE_CHECK(cudaMemcpyAsync(sc.x, x + (size_t)t0 * H, sizeof(float) * n * H, cudaMemcpyHostToDevice, s));
+        if (run_route(m, sc.x, n, sc, s)) return -1;
+        QE_CHECK(cudaMemcpyAsync(idx + (size_t)t0 * k, sc.idx, 4 * n * k, cudaMemcpyDeviceToHost, s));
+        QE_CHECK(cudaMemcpyAsync(score + (size_t)t0 * k, sc.score, 4 * n * k, cudaMemcpyDeviceToHost, s));
+        QE_CHECK(cudaStreamSynchronize(s));
+    }
+    return 0;
+}
+
+int qe_qmat_matvec(const uint32_t *w, const uint16_t *scales, const uint16_t *biases, int rows, int cols, int bits,
+                   int group_size, const float *x, float *y) {
+    /* validation exactly as engine/src/qmat.c:16-22 (y untouched on error) */
+    if (!w || !scales || !biases || !x || !y) return -1;
+    if (bits != 4 && bits != 8) return -1;
+    if (group_size != 32 && group_size != 64 && group_size != 128) return -1;
+    if (rows <= 0 || cols <= 0) return -1;
+    if (cols % group_size != 0) return -1;
+    if (cols / group_size > 4096) return -1;
+    DevCtx *d;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev_ctx(dev, &d)) return -1;
+    cudaStream_t s = d->stream;
+    const size_t wb = (size_t)rows * ((size_t)cols * bits / 32) * 4, gb = (size_t)rows * (cols / group_size) * 2;
+    char *buf = nullptr;
+    const size_t total = align256(wb) + 2 * align256(gb) + align256(4 * (size_t)cols) + align256(4 * (size_t)rows);
+    QE_CHECK(cudaMalloc((void **)&buf, total));
+    QeQDev q;
+    q.w = (const uint32_t *)buf;
+    q.scales = (const uint16_t *)(buf + align256(wb));
+    q.biases = (const uint16_t *)(buf + align256(wb) + align256(gb));
+    float *dx = (float *)(buf + align256(wb) + 2 * align256(gb));
+    float *dy = (float *)((char *)dx + align256(4 * (size_t)cols));
+    q.rows = rows; q.cols = cols; q.bits = bits; q.group_size = group_size;
+    int rc = cudaMemcpyAsync((void *)q.w, w, wb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+             cudaMemcpyAsync((void *)q.scales, scales, gb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+             cudaMemcpyAsync((void *)q.biases, biases, gb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+             cudaMemcpyAsync(dx, x, 4 * (size_t)cols, cudaMemcpyHostToDevice, s) != cudaSuccess;
+    if (!rc) rc = qe_launch_qmatvec(&q, dx, 1, dy, s);
+    if (!rc) rc = cudaMemcpyAsync(y, dy, 4 * (size_t)rows, cudaMemcpyDeviceToHost, s) != cudaSuccess;
+    if (!rc) rc = cudaStreamSynchronize(s) != cudaSuccess;
+    cudaFree(buf);
+    return rc ? -1 : 0;
+}
+
+int qe_route_logits(int T, int E, int k, const float *logits, float *probs, int32_t *idx, float *score) {
+    if (T < 1 || !logits || !idx || !score) return -1;
+    if (E < 1 || E > 512 || k < 1 || k > 16 || k > E) return -1;
+    DevCtx *d;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev_ctx(dev, &d)) return -1;
+    cudaStream_t s = d->stream;
+    char *buf = nullptr;
+    const size_t lb = align256(4 * (size_t)T * E), kb = align256(4 * (size_t)T * k);
+    QE_CHECK(cudaMalloc((void **)&buf, 2 * lb + 2 * kb));
+    float *dl = (float *)buf, *dp = (float *)(buf + lb), *ds = (float *)(buf + 2 * lb);
+    int32_t *di = (int32_t *)(buf + 2 * lb + kb);
+    int rc = cudaMemcpyAsync(dl, logits, 4 * (size_t)T * E, cudaMemcpyHostToDevice, s) != cudaSuccess;
+    if (!rc) rc = qe_launch_route_topk(dl, E, T, E, k, di, ds, dp, s);
+    if (!rc && probs) rc = cudaMemcpyAsync(probs, dp, 4 * (size_t)T * E, cudaMemcpyDeviceToHost, s) != cudaSuccess;
+    if (!rc) rc = cudaMemcpyAsync(idx, di, 4 * (size_t)T * k, cudaMemcpyDeviceToHost, s) != cudaSuccess;
+    if (!rc) rc = cudaMemcpyAsync(score, ds, 4 * (size_t)T * k, cudaMemcpyDeviceToHost, s) != cudaSuccess;
+    if (!rc) rc = cudaStreamSynchronize(s) != cudaSuccess;
+    cudaFree(buf);
+    return rc ? -1 : 0;
+}
+
+static int run_op(int op, float *out, const float *a, const float *b, int n) {
+    if (n < 1 || !out || !a || (op == 0 && !b)) return -1;
+    DevCtx *d;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev_ctx(dev, &d)) return -1;
+    cudaStream_t s = d->stream;
+    float *buf = nullptr;
+    const size_t nb = align256(4 * (size_t)n);
+    QE_CHECK(cudaMalloc((void **)&buf, 3 * nb));
+    float *da = buf, *db = (float *)((char *)buf + nb), *dout = (float *)((char *)buf + 2 * nb);
+    int rc = cudaMemcpyAsync(da, a, 4 * (size_t)n, cudaMemcpyHostToDevice, s) != cudaSuccess;
+    if (!rc && op == 0) rc = cudaMemcpyAsync(db, b, 4 * (size_t)n, cudaMemcpyHostToDevice, s) != cudaSuccess;
+    if (!rc) {
+        ops_kernel<<<(n + 255) / 256, 256, 0, s>>>(op, da, db, dout, n);
+        rc = cudaGetLastError() != cudaSuccess;
+    }
+    if (!rc) rc = cudaMemcpyAsync(out, dout, 4 * (size_t)n, cudaMemcpyDeviceToHost, s) != cudaSuccess;
+    if (!rc) rc = cudaStreamSynchronize(s) != cudaSuccess;
+    cudaFree(buf);
+    return rc ? -1 : 0;
+}
+
+int qe_op_silu_mul(float *out, const float *gate, const float *up, int n) { return run_op(0, out, gate, up, n); }
+int qe_op_sigmoid(float *out, const float *x, int n) { return run_op(1, out, x, nullptr, n); }
+int qe_op_expf(float *out, const float *x, int n) { return run_op(2, out, x, nullptr, n); }
+
+int qe_profile_begin(int device) {
+    if (device < 0 || device >= 64) return -1;
+    g_prof[device].on = true;
+    g_prof[device].used = 0;
+    return 0;
+}
+
+int qe_profile_end(int device, double *stage_ms, int *passes) {
+    if (device < 0 || device >= 64) return -1;
+    Prof &p = g_prof[device];
+    p.on = false;
+    for (int i = 0; i < kStages; i++) stage_ms[i] = 0.0;
+    const size_t per = kStages + 1;
+    const size_t n = p.used / per;
+    QE_CHECK(cudaSetDevice(device));
+    for (size_t k = 0; k < n; k++) {
+        QE_CHECK(cudaEventSynchronize(p.pool[k * per + kStages]));
+        for (int i = 0; i < kStages; i++) {
+            float ms = 0.0f;
+            QE_CHECK(cudaEventElapsedTime(&ms, p.pool[k * per + i], p.pool[k * per + i + 1]));
+            stage_ms[i] += ms;
+        }
+    }
+    if (passes) *passes = (int)n;
+    p.used = 0;
+    return 0;
+}
+
+unsigned long long qe_kernel_launches(void) { return g_launches.load(); }
+
+double qe_expert_gb_read(void) { return (double)g_bytes_read.load() / 1e9; }
+double qe_expert_read_seconds(void) { return g_gpu_seconds; }
+int qe_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+    return n;
+}
+
+}  // extern "C"

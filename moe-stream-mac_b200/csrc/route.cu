@@ -1,0 +1,391 @@
+/* route.cu: router logits, softmax, top-k and renormalisation, bit-exact with the reference.
+ *
+ * Reference: engine/src/moe_layer.c:29-37 (route), engine/src/ops.c:29-73 (op_softmax, op_topk).
+ *
+ * fp32 router (the benchmark configurations): the reference has no fp32 router, so the order of the
+ * dot product is defined once and followed by the CPU checker (or_dot_f32 in oracle/moe_oracle.c):
+ * 64-input fmaf chains starting from 0 in ascending index order, the chunk sums added in chunk order
+ * to a total that starts at 0.0f. Both kernels below evaluate exactly that sequence of IEEE operations.
+ * Quantized router (checkpoints): qmat_matvec's order (qmat.c:27-44, qgroup.c:48-53) without FMA.
+ */
+#include "qe_common.cuh"
+#include "qe_kernels.h"
+
+namespace {
+
+constexpr int kChunk = 64;        /* fp32 router chunk length (or_dot_f32) */
+constexpr int kMaxLaneChunks = 4; /* hidden <= 32 * 4 * 64 = 8192 */
+constexpr int kGemvTokens = 8;
+
+/* Decode / small batch: one warp per router row (E routed rows + the shared gate row). Lane c owns
+ * chunks c, c+32, ...; each chunk is an fmaf chain per token; lane 0..nt-1 then add the chunk sums in
+ * chunk order. */
+__global__ void __launch_bounds__(128) router_gemv_f32_kernel(const float *__restrict__ W,
+                                                              const float *__restrict__ bias,
+                                                              const float *__restrict__ x, int T, int H, int E,
+                                                              float *__restrict__ logits) {
+    const int lane = threadIdx.x & 31;
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (row > E) return;
+    const float *w = W + (size_t)row * H;
+    const int nch = (H + kChunk - 1) / kChunk;
+    const int ld = E + 1;
+    for (int t0 = 0; t0 < T; t0 += kGemvTokens) {
+        const int nt = min(kGemvTokens, T - t0);
+        float acc[kMaxLaneChunks][kGemvTokens];
+#pragma unroll
+        for (int cc = 0; cc < kMaxLaneChunks; cc++) {
+#pragma unroll
+            for (int t = 0; t < kGemvTokens; t++) acc[cc][t] = 0.0f;
+            const int c = lane + 32 * cc;
+            if (c < nch) {
+                const int i0 = c * kChunk, i1 = min(i0 + kChunk, H);
+                for (int i = i0; i < i1; i++) {
+                    const float wv = __ldg(w + i);
+#pragma unroll
+                    for (int t = 0; t < kGemvTokens; t++)
+                        if (t < nt) acc[cc][t] = __fmaf_rn(wv, __ldg(x + (size_t)(t0 + t) * H + i), acc[cc][t]);
+                }
+            }
+        }
+        float total[kGemvTokens];
+#pragma unroll
+        for (int t = 0; t < kGemvTokens; t++) total[t] = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < kMaxLaneChunks; cc++) {
+            if (cc * 32 >= nch) break;
+            for (int src = 0; src < 32; src++) {
+                if (cc * 32 + src >= nch) break;
+#pragma unroll
+                for (int t = 0; t < kGemvTokens; t++) {
+                    const float v = __shfl_sync(QE_FULL, acc[cc][t], src);
+                    total[t] = __fadd_rn(total[t], v);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < kGemvTokens; t++) {
+            if (lane == t && t < nt) {
+                float l = total[t];
+                if (bias && row < E) l = __fadd_rn(l, bias[row]);
+                logits[(size_t)(t0 + t) * ld + row] = l;
+            }
+        }
+    }
+}
+
+/* Prefill: 64 rows x 32 tokens per CTA, 256 threads, 4 rows x 2 tokens per thread. The K loop runs in
+ * 64-input chunks; within a chunk every accumulator is an fmaf chain in ascending k, and at the end of
+ * the chunk it is added to the running total, which is exactly or_dot_f32's order. */
+constexpr int kGR = 64, kGT = 32;
+__global__ void __launch_bounds__(256) router_gemm_f32_kernel(const float *__restrict__ W,
+                                                              const float *__restrict__ bias,
+                                                              const float *__restrict__ x, int T, int H, int E,
+                                                              float *__restrict__ logits) {
+    __shared__ __align__(16) float Ws[kChunk][kGR];   /* [k][row] */
+    __shared__ __align__(16) float Xs[kChunk][kGT];   /* [k][token] */
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int r0 = blockIdx.x * kGR, t0 = blockIdx.y * kGT;
+    const int Ep1 = E + 1;
+    float total[4][2], acc[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) total[i][j] = 0.0f;
+    for (int k0 = 0; k0 < H; k0 += kChunk) {
+        const int kn = min(kChunk, H - k0);
+        /* W tile: 64 rows x 64 k, transposed into Ws[k][row] */
+        for (int e = tid; e < kGR * kChunk; e += 256) {
+            const int r = e / kChunk, k = e % kChunk;
+            const int gr = r0 + r;
+            Ws[k][r] = (gr < Ep1 && k < kn) ? __ldg(W + (size_t)gr * H + k0 + k) : 0.0f;
+        }
+        for (int e = tid; e < kGT * kChunk; e += 256) {
+            const int t = e / kChunk, k = e % kChunk;
+            const int gt = t0 + t;
+            Xs[k][t] = (gt < T && k < kn) ? __ldg(x + (size_t)gt * H + k0 + k) : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) acc[i][j] = 0.0f;
+        for (int k = 0; k < kn; k++) {
+            const float4 wv = *reinterpret_cast<const float4 *>(&Ws[k][ty * 4]);
+            const float2 xv = *reinterpret_cast<const float2 *>(&Xs[k][tx * 2]);
+            const float wr[4] = {wv.x, wv.y, wv.z, wv.w};
+            const float xr[2] = {xv.x, xv.y};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) acc[i][j] = __fmaf_rn(wr[i], xr[j], acc[i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) total[i][j] = __fadd_rn(total[i][j], acc[i][j]);
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = r0 + ty * 4 + i;
+        if (r >= Ep1) continue;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int t = t0 + tx * 2 + j;
+            if (t >= T) continue;
+            float l = total[i][j];
+            if (bias && r < E) l = __fadd_rn(l, bias[r]);
+            logits[(size_t)t * Ep1 + r] = l;
+        }
+    }
+}
+
+/* Quantized router in qmat_matvec's exact order: one warp per (row, token); lane g owns groups g, g+32,
+ * ...: gsum_g and sum_q_g are sequential float sums (qmat.c:27-32, qgroup.c:48-53), then
+ * t_g = scale*sum_q + bias*gsum and lane 0 adds the t_g in group order (qmat.c:41-44). */
+__global__ void router_qmat_exact_kernel(QeQDev m, int row_base, const float *__restrict__ x, int T, int H,
+                                         int ld, float *__restrict__ logits) {
+    const int lane = threadIdx.x & 31;
+    const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int row = (int)(wid % m.rows), t = (int)(wid / m.rows);
+    if (t >= T) return;
+    const int gs = m.group_size, bits = m.bits, per = 32 / bits, ng = m.cols / gs;
+    const uint32_t mask = (1u << bits) - 1u;
+    const int wpr = m.cols * bits / 32, wpg = gs * bits / 32;
+    const uint32_t *wp = m.w + (size_t)row * wpr;
+    const float *xv = x + (size_t)t * H;
+    float total = 0.0f;
+    for (int g0 = 0; g0 < ng; g0 += 32) {
+        const int g = g0 + lane;
+        float tg = 0.0f;
+        if (g < ng) {
+            float gsum = 0.0f, sq = 0.0f;
+            for (int i = 0; i < gs; i++) gsum = __fadd_rn(gsum, xv[g * gs + i]);
+            const uint32_t *gw = wp + (size_t)g * wpg;
+            for (int j = 0; j < gs; j++) {
+                const float q = (float)((gw[j / per] >> ((j % per) * bits)) & mask);
+                sq = __fadd_rn(sq, __fmul_rn(q, xv[g * gs + j]));
+            }
+            const float s = qe_bf16_to_f32(m.scales[(size_t)row * ng + g]);
+            const float b = qe_bf16_to_f32(m.biases[(size_t)row * ng + g]);
+            tg = __fadd_rn(__fmul_rn(s, sq), __fmul_rn(b, gsum));
+        }
+        const int nsrc = min(32, ng - g0);
+        for (int src = 0; src < nsrc; src++) total = __fadd_rn(total, __shfl_sync(QE_FULL, tg, src));
+    }
+    if (lane == 0) logits[(size_t)t * ld + row_base + row] = total;
+}
+
+/* ---------------------------------------------------------------------------------------------------
+ * Softmax + top-k + renormalisation: one warp per token, bit-exact with ops.c:29-73 + moe_layer.c:31-36.
+ *   max     : order-independent for non-NaN input (a NaN anywhere takes the sequential path).
+ *   e_i     : qe_expf(x_i - max), identical to the host expf.
+ *   sum     : ops.c adds the e_i in DOUBLE in index order. The warp adds them pairwise in double and
+ *             proves that rounding to float gives the same value: the sequential and the pairwise sums
+ *             each lie within (n-1)u*S of the exact sum (u = 2^-53, all terms positive), so if the
+ *             interval [S_pair - B, S_pair + B], B = (2n+8) u S_pair, lies strictly inside the rounding
+ *             interval of f = (float)S_pair, then (float)S_seq == f. Otherwise (probability ~ n*2^-29)
+ *             lane 0 repeats the sum sequentially.
+ *   p_i     : e_i / (float)sum, IEEE division.
+ *   top-k   : op_topk's insertion sort keeps values in descending order and equal values in index
+ *             order, and at capacity admits only a strictly larger value; for non-NaN input that is the
+ *             first k of the order (p desc, index asc), found here by k rounds of warp arg-max.
+ *   score_i : p_sel_i / (float sum of p_sel in top-k order).
+ * ------------------------------------------------------------------------------------------------- */
+constexpr int kMaxEPL = 16; /* E <= 512 */
+constexpr int kRouteWarps = 4;
+
+__device__ void route_token_sequential(const float *lg, int E, int k, float *probs_s, int *idx_s, int32_t *idx,
+                                       float *score, float *probs_out) {
+    /* ops.c:29-42 literally */
+    float max_val = lg[0];
+    for (int i = 1; i < E; i++)
+        if (lg[i] > max_val) max_val = lg[i];
+    double sum = 0.0;
+    for (int i = 0; i < E; i++) {
+        probs_s[i] = qe_expf(__fsub_rn(lg[i], max_val));
+        sum = __dadd_rn(sum, (double)probs_s[i]);
+    }
+    const float sf = __double2float_rn(sum);
+    for (int i = 0; i < E; i++) probs_s[i] = __fdiv_rn(probs_s[i], sf);
+    /* ops.c:44-73 literally */
+    int count = 0;
+    for (int i = 0; i < E; i++) {
+        const float val = probs_s[i];
+        int pos = count;
+        while (pos > 0 && probs_s[idx_s[pos - 1]] < val) pos--;
+        if (count == k) {
+            if (probs_s[idx_s[k - 1]] < val) {
+                for (int j = k - 1; j > pos; j--) idx_s[j] = idx_s[j - 1];
+                idx_s[pos] = i;
+            }
+        } else {
+            for (int j = count; j > pos; j--) idx_s[j] = idx_s[j - 1];
+            idx_s[pos] = i;
+            count++;
+        }
+    }
+    float s = 0.0f;
+    for (int i = 0; i < k; i++) s = __fadd_rn(s, probs_s[idx_s[i]]);
+    for (int i = 0; i < k; i++) {
+        idx[i] = idx_s[i];
+        score[i] = __fdiv_rn(probs_s[idx_s[i]], s);
+    }
+    if (probs_out)
+        for (int i = 0; i < E; i++) probs_out[i] = probs_s[i];
+}
+
+__global__ void __launch_bounds__(kRouteWarps * 32) route_topk_kernel(const float *__restrict__ logits, int ld,
+                                                                      int T, int E, int k,
+                                                                      int32_t *__restrict__ idx_out,
+                                                                      float *__restrict__ score_out,
+                                                                      float *__restrict__ probs_out) {
+    extern __shared__ float smem[];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int t = blockIdx.x * kRouteWarps + w;
+    if (t >= T) return;
+    float *probs_s = smem + (size_t)w * 2 * E;   /* [E] */
+    int *idx_s = reinterpret_cast<int *>(probs_s + E);
+    const float *lg = logits + (size_t)t * ld;
+    const int epl = (E + 31) / 32;
+
+    float v[kMaxEPL];
+    bool has_nan = false;
+    float mx = -__int_as_float(0x7f800000);
+#pragma unroll
+    for (int i = 0; i < kMaxEPL; i++) {
+        const int e = lane + 32 * i;
+        v[i] = (i < epl && e < E) ? lg[e] : 0.0f;
+        if (i < epl && e < E) {
+            has_nan |= (v[i] != v[i]);
+            mx = fmaxf(mx, v[i]);
+        }
+    }
+    has_nan = __any_sync(QE_FULL, has_nan);
+    if (has_nan) {
+        if (lane == 0)
+            route_token_sequential(lg, E, k, probs_s, idx_s, idx_out + (size_t)t * k, score_out + (size_t)t * k,
+                                   probs_out ? probs_out + (size_t)t * E : nullptr);
+        return;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(QE_FULL, mx, o));
+
+    double part = 0.0;
+#pragma unroll
+    for (int i = 0; i < kMaxEPL; i++) {
+        const int e = lane + 32 * i;
+        if (i < epl && e < E) {
+            v[i] = qe_expf(__fsub_rn(v[i], mx));
+            part = __dadd_rn(part, (double)v[i]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(QE_FULL, part, o));
+    float sf = __double2float_rn(part);
+    {
+        const double B = (double)(2 * E + 8) * 0x1p-53 * part;
+        const float up = nextafterf(sf, __int_as_float(0x7f800000)), dn = nextafterf(sf, 0.0f);
+        const double mid_hi = ((double)sf + (double)up) * 0.5, mid_lo = ((double)sf + (double)dn) * 0.5;
+        const bool safe = (part - B > mid_lo) && (part + B < mid_hi);
+        if (!safe) { /* uniform across the warp: every lane holds the same part */
+#pragma unroll
+            for (int i = 0; i < kMaxEPL; i++) {
+                const int e = lane + 32 * i;
+                if (i < epl && e < E) probs_s[e] = v[i];
+            }
+            __syncwarp();
+            double seq = 0.0;
+            if (lane == 0)
+                for (int e = 0; e < E; e++) seq = __dadd_rn(seq, (double)probs_s[e]);
+            seq = __shfl_sync(QE_FULL, seq, 0);
+            sf = __double2float_rn(seq);
+            __syncwarp();
+        }
+    }
+    unsigned used = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxEPL; i++) {
+        const int e = lane + 32 * i;
+        if (i < epl && e < E) {
+            v[i] = __fdiv_rn(v[i], sf);
+            if (probs_out) probs_out[(size_t)t * E + e] = v[i];
+        } else {
+            used |= 1u << i; /* not a candidate */
+        }
+    }
+    float psel = 0.0f, ssum = 0.0f;
+    int isel = 0;
+    for (int r = 0; r < k; r++) {
+        float bv = -__int_as_float(0x7f800000);
+        int bi = 0x7fffffff, bslot = -1;
+#pragma unroll
+        for (int i = 0; i < kMaxEPL; i++) {
+            if (!(used >> i & 1u) && (bslot < 0 || v[i] > bv)) { /* ascending i = ascending index */
+                bv = v[i];
+                bi = lane + 32 * i;
+                bslot = i;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(QE_FULL, bv, o);
+            const int oi = __shfl_xor_sync(QE_FULL, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bslot >= 0 && bi == lane + 32 * bslot) used |= 1u << bslot;
+        ssum = __fadd_rn(ssum, bv);
+        if (lane == r) {
+            psel = bv;
+            isel = bi;
+        }
+    }
+    if (lane < k) {
+        idx_out[(size_t)t * k + lane] = isel;
+        score_out[(size_t)t * k + lane] = __fdiv_rn(psel, ssum);
+    }
+}
+
+}  // namespace
+
+int qe_launch_router_f32(const float *W, const float *bias, const float *x, int T, int H, int E, float *logits,
+                         cudaStream_t s) {
+    if (H > 32 * kMaxLaneChunks * kChunk) QE_FAIL("router: hidden %d too large", H);
+    if (T <= 16) {
+        const int rows = E + 1, warps_per_block = 4;
+        router_gemv_f32_kernel<<<(rows + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, s>>>(
+            W, bias, x, T, H, E, logits);
+    } else {
+        dim3 grid((E + 1 + kGR - 1) / kGR, (T + kGT - 1) / kGT);
+        router_gemm_f32_kernel<<<grid, 256, 0, s>>>(W, bias, x, T, H, E, logits);
+    }
+    QE_CHECK(cudaGetLastError());
+    return 0;
+}
+
+int qe_launch_router_qmat(const QeQDev *router, const QeQDev *sh_router, const float *x, int T, int H, int E,
+                          float *logits, cudaStream_t s) {
+    const long long warps = (long long)router->rows * T;
+    router_qmat_exact_kernel<<<(unsigned)((warps + 3) / 4), 128, 0, s>>>(*router, 0, x, T, H, E + 1, logits);
+    QE_CHECK(cudaGetLastError());
+    if (sh_router) {
+        router_qmat_exact_kernel<<<(T + 3) / 4, 128, 0, s>>>(*sh_router, E, x, T, H, E + 1, logits);
+        QE_CHECK(cudaGetLastError());
+    }
+    return 0;
+}
+
+int qe_launch_route_topk(const float *logits, int ld, int T, int E, int k, int32_t *idx, float *score,
+                         float *probs, cudaStream_t s) {
+    if (E < 1 || E > 32 * kMaxEPL) QE_FAIL("route: E=%d outside [1, %d]", E, 32 * kMaxEPL);
+    if (k < 1 || k > 16 || k > E) QE_FAIL("route: top_k=%d outside [1, min(16, E)]", k);
+    const size_t smem = (size_t)kRouteWarps * 2 * E * sizeof(float);
+    route_topk_kernel<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, smem, s>>>(logits, ld, T, E, k, idx,
+                                                                                        score, probs);
+    QE_CHECK(cudaGetLastError());
+    return 0;
+}

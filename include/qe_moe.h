@@ -119,6 +119,8 @@ int qe_profile_begin(int device);
 int qe_profile_end(int device, double *stage_ms, int *passes);
 /* Kernels launched by this library since process start. */
 unsigned long long qe_kernel_launches(void);
+/* Nonzero if a tensor-core kernel's pipeline wait timed out (it then returned early; outputs invalid). */
+int qe_device_error(void);
 
 #ifdef __cplusplus
 }

@@ -60,4 +60,18 @@ int qe_launch_synth_normal(uint64_t seed, uint32_t block, uint32_t stream, size_
 
 int qe_num_sms(void);
 
+/* Tensor-core (tcgen05) prefill path, expert_tc.cu. */
+#include <cuda_bf16.h>
+bool qe_tc_supported(const QeExpertArgs *a);
+size_t qe_tc_map_bytes(void);
+int qe_tc_weight_maps(const QeQDev *q, int n_experts, void *codes_map, void *sc_map, void *bi_map);
+int qe_launch_tc_gateup(const QeExpertArgs *a, const void *maps, const float *x, const QeBuckets *b, int T,
+                        __nv_bfloat16 *act, float *actsum, __nv_bfloat16 *h3s, float *h3sum, int ldh, int grid,
+                        cudaStream_t s);
+int qe_launch_tc_down(const QeExpertArgs *a, const void *maps, const __nv_bfloat16 *h3s, const float *h3sum, int ldh,
+                      const QeBuckets *b, int T, float *ybuf, int grid, cudaStream_t s);
+int qe_tc_error(void);
+int qe_tc_bm(void);
+int qe_tc_bn(void);
+
 #endif

@@ -25,6 +25,9 @@
 
 int qe_expert_rows_per_cta(void);
 
+/* Batches of at least this many tokens take the tensor-core (tcgen05) expert path when the shape allows. */
+static constexpr int kTcMinTokens = 64;
+
 /* ------------------------------------------------------------------ per-device context and workspace */
 
 namespace {
@@ -111,6 +114,8 @@ struct Scratch {
     float *x, *out, *logits, *score, *h3, *ybuf;
     int32_t *idx;
     QeBuckets b;
+    __nv_bfloat16 *act, *h3s;   /* tensor-core path: split activations [3][npairs][K] */
+    float *actsum, *h3sum;      /* per-(pair, group of 64) sums */
 };
 
 size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
@@ -137,6 +142,10 @@ size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
     t.b.slot_expert = (int32_t *)take(sizeof(int32_t) * (E + 2));
     t.b.slot_items = (int32_t *)take(sizeof(int32_t) * 2 * (E + 2));
     t.b.n_active = (int32_t *)take(sizeof(int32_t) * 4);
+    t.act = (__nv_bfloat16 *)take(2 * 3 * npair * c.hidden);
+    t.actsum = (float *)take(4 * npair * (c.hidden / 64 + 1));
+    t.h3s = (__nv_bfloat16 *)take(2 * 3 * npair * I);
+    t.h3sum = (float *)take(4 * npair * (I / 64 + 1));
     if (s) *s = t;
     return off;
 }
@@ -155,6 +164,10 @@ struct QeMoe {
     QeQDev router_q, sh_router_q;
     QeExpertArgs ex;
     size_t expert_bytes;    /* bytes of one routed expert (gate+up+down codes, scales, biases) */
+    int path;               /* 0 = auto, 1 = mma.sync only, 2 = tensor-core (tcgen05) whenever supported */
+    bool tc;                /* tensor-core path available for this shape */
+    alignas(64) unsigned char maps_gu[2 * 2 * 3 * 128];  /* [routed/shared][gate/up][codes, scales, biases] */
+    alignas(64) unsigned char maps_dn[2 * 3 * 128];      /* [routed/shared][codes, scales, biases] */
 };
 
 namespace {
@@ -187,8 +200,9 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     if (validate(c)) return nullptr;
     DevCtx *d;
     if (dev_ctx(c->device, &d)) return nullptr;
-    QeMoe *m = (QeMoe *)calloc(1, sizeof(QeMoe));
+    QeMoe *m = (QeMoe *)aligned_alloc(64, (sizeof(QeMoe) + 63) & ~(size_t)63);
     if (!m) return nullptr;
+    memset(m, 0, sizeof(QeMoe));
     m->cfg = *c;
     if (m->cfg.max_tokens < 1) m->cfg.max_tokens = 4096;
     m->device = c->device;
@@ -232,6 +246,22 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     m->ex.E = E; m->ex.k = c->top_k; m->ex.hidden = H; m->ex.inter = I; m->ex.sh_inter = Is;
     size_t wb, gb;
     m->expert_bytes = qbytes(1, I, H, b, gs, &wb, &gb) * 2 + qbytes(1, H, I, b, gs, &wb, &gb);
+    const char *path = getenv("QE_EXPERT_PATH");   /* auto (default) | mma | tc */
+    m->path = path && !strcmp(path, "mma") ? 1 : path && !strcmp(path, "tc") ? 2 : 0;
+    m->tc = qe_tc_supported(&m->ex);
+    if (m->tc) {
+        const size_t mb = qe_tc_map_bytes();
+        const QeQDev *gu[2][2] = {{&m->ex.gate, &m->ex.up}, {&m->ex.sh_gate, &m->ex.sh_up}};
+        const QeQDev *dn[2] = {&m->ex.down, &m->ex.sh_down};
+        for (int r = 0; r < 2 && m->tc; r++) {
+            for (int q = 0; q < 2 && m->tc; q++) {
+                unsigned char *o = m->maps_gu + ((r * 2 + q) * 3) * mb;
+                m->tc = !qe_tc_weight_maps(gu[r][q], r ? 1 : E, o, o + mb, o + 2 * mb);
+            }
+            unsigned char *o = m->maps_dn + (r * 3) * mb;
+            if (m->tc) m->tc = !qe_tc_weight_maps(dn[r], r ? 1 : E, o, o + mb, o + 2 * mb);
+        }
+    }
     return m;
 }
 
@@ -412,6 +442,24 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     if (qe_launch_route_topk(sc.logits, c.E + 1, T, c.E, c.top_k, sc.idx, sc.score, nullptr, s)) return -1;
     g_launches += 1;
     prof_mark(dev, s);
+    const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
+    const bool use_tc = m->tc && (m->path == 2 || (m->path == 0 && T >= kTcMinTokens));
+    if (use_tc) {
+        const int R = qe_tc_bm(), NB = qe_tc_bn();
+        const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
+                  tiles_dn = (c.hidden + R - 1) / R;
+        if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s)) return -1;
+        prof_mark(dev, s);
+        if (qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, T, sc.act, sc.actsum, sc.h3s, sc.h3sum, I, sms, s))
+            return -1;
+        prof_mark(dev, s);
+        if (qe_launch_tc_down(&m->ex, m->maps_dn, sc.h3s, sc.h3sum, I, &sc.b, T, sc.ybuf, sms, s)) return -1;
+        prof_mark(dev, s);
+        if (qe_launch_combine(sc.ybuf, sc.score, sc.logits, c.E + 1, T, c.E, c.top_k, c.hidden, out, s)) return -1;
+        prof_mark(dev, s);
+        g_launches += 5;
+        return 0;
+    }
     const int R = qe_expert_rows_per_cta();
     const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R, tiles_dn = (c.hidden + R - 1) / R;
     const int chunk = T < 8 ? T : 8;
@@ -423,7 +471,6 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     const int tmax = std::max(tiles_gu, tiles_sh);
     const int grid_gu = (int)std::min<long long>(chunks * tmax, 16LL * sms);
     const int grid_dn = (int)std::min<long long>(chunks * tiles_dn, 16LL * sms);
-    const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
     if (qe_launch_gateup(&m->ex, x, &sc.b, T, sc.h3, I, grid_gu, s)) return -1;
     prof_mark(dev, s);
     if (qe_launch_down(&m->ex, sc.h3, I, &sc.b, T, sc.ybuf, grid_dn, s)) return -1;
@@ -647,6 +694,8 @@ int qe_profile_end(int device, double *stage_ms, int *passes) {
 }
 
 unsigned long long qe_kernel_launches(void) { return g_launches.load(); }
+
+int qe_device_error(void) { return qe_tc_error(); }
 
 double qe_expert_gb_read(void) { return (double)g_bytes_read.load() / 1e9; }
 double qe_expert_read_seconds(void) { return g_gpu_seconds; }

@@ -68,6 +68,7 @@ def lib() -> C.CDLL:
         L.qe_profile_begin.argtypes = [C.c_int]
         L.qe_profile_end.argtypes = [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         L.qe_kernel_launches.restype = C.c_ulonglong
+        L.qe_device_error.restype = C.c_int
         _lib = L
     return _lib
 

@@ -142,7 +142,7 @@ __device__ void stage_rows(const float *const *rows, int nt, int K, uint32_t *xs
 /* One warp: out[4] (rows g, g+8 x tokens 2t, 2t+1) += W[16 rows] . x, full K. */
 template <int BITS, int GS, int NMAT>
 __device__ __forceinline__ void warp_qmm(const QeQDev *const mats[NMAT], const size_t row_word[NMAT][2],
-                                         const size_t row_grp[NMAT][2], const bool row_ok[2], int ng,
+                                         const size_t row_grp[NMAT][2], size_t grp_stride, const bool row_ok[2], int ng,
                                          const uint32_t *xs, const float *xsum, int tstride, int nt,
                                          float (&acc)[NMAT][4]) {
     using G = Geo<BITS, GS>;
@@ -199,8 +199,8 @@ __device__ __forceinline__ void warp_qmm(const QeQDev *const mats[NMAT], const s
             for (int r = 0; r < 2; r++) {
                 float sc = 0.0f, bi = 0.0f;
                 if (row_ok[r]) {
-                    sc = qe_bf16_to_f32(__ldg(mats[m]->scales + row_grp[m][r] + g));
-                    bi = qe_bf16_to_f32(__ldg(mats[m]->biases + row_grp[m][r] + g));
+                    sc = qe_bf16_to_f32(__ldg(mats[m]->scales + row_grp[m][r] + g * grp_stride));
+                    bi = qe_bf16_to_f32(__ldg(mats[m]->biases + row_grp[m][r] + g * grp_stride));
                 }
                 acc[m][2 * r] = __fadd_rn(acc[m][2 * r], __fmaf_rn(sc, p[m][2 * r], __fmul_rn(bi, xs0)));
                 acc[m][2 * r + 1] = __fadd_rn(acc[m][2 * r + 1], __fmaf_rn(sc, p[m][2 * r + 1], __fmul_rn(bi, xs1)));
@@ -271,16 +271,18 @@ __global__ void __launch_bounds__(kWarps * 32) expert_kernel(QeExpertArgs a, con
             const size_t wpr = (size_t)K * BITS / 32, gpr = (size_t)K / GS;
             const size_t ebase = shared ? 0 : (size_t)e * rows_total;
             size_t rw[2][2], rg[2][2];
+            const size_t eg = shared ? 0 : (size_t)e;
 #pragma unroll
             for (int m = 0; m < 2; m++)
 #pragma unroll
                 for (int r = 0; r < 2; r++) {
-                    const size_t row = ebase + (size_t)(row_ok[r] ? r_base + gq + 8 * r : 0);
-                    rw[m][r] = row * wpr;
-                    rg[m][r] = row * gpr;
+                    const size_t rin = (size_t)(row_ok[r] ? r_base + gq + 8 * r : 0);
+                    rw[m][r] = (ebase + rin) * wpr;
+                    rg[m][r] = mats[m]->scale_t ? eg * gpr * rows_total + rin : (ebase + rin) * gpr;
                 }
             float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-            warp_qmm<BITS, GS, 2>(mats, rw, rg, row_ok, ng, xs, xsum, tstride, nt, acc);
+            warp_qmm<BITS, GS, 2>(mats, rw, rg, mats[0]->scale_t ? (size_t)rows_total : 1, row_ok, ng, xs, xsum,
+                                  tstride, nt, acc);
 #pragma unroll
             for (int r = 0; r < 2; r++)
 #pragma unroll
@@ -296,14 +298,16 @@ __global__ void __launch_bounds__(kWarps * 32) expert_kernel(QeExpertArgs a, con
             const size_t wpr = (size_t)K * BITS / 32, gpr = (size_t)K / GS;
             const size_t ebase = shared ? 0 : (size_t)e * rows_total;
             size_t rw[1][2], rg[1][2];
+            const size_t eg = shared ? 0 : (size_t)e;
 #pragma unroll
             for (int r = 0; r < 2; r++) {
-                const size_t row = ebase + (size_t)(row_ok[r] ? r_base + gq + 8 * r : 0);
-                rw[0][r] = row * wpr;
-                rg[0][r] = row * gpr;
+                const size_t rin = (size_t)(row_ok[r] ? r_base + gq + 8 * r : 0);
+                rw[0][r] = (ebase + rin) * wpr;
+                rg[0][r] = mats[0]->scale_t ? eg * gpr * rows_total + rin : (ebase + rin) * gpr;
             }
             float acc[1][4] = {{0, 0, 0, 0}};
-            warp_qmm<BITS, GS, 1>(mats, rw, rg, row_ok, ng, xs, xsum, tstride, nt, acc);
+            warp_qmm<BITS, GS, 1>(mats, rw, rg, mats[0]->scale_t ? (size_t)rows_total : 1, row_ok, ng, xs, xsum,
+                                  tstride, nt, acc);
 #pragma unroll
             for (int r = 0; r < 2; r++)
 #pragma unroll
@@ -391,10 +395,10 @@ __global__ void __launch_bounds__(kWarps * 32) qmat_kernel(QeQDev m, const float
     for (int r = 0; r < 2; r++) {
         const size_t row = (size_t)(row_ok[r] ? r_base + gq + 8 * r : 0);
         rw[0][r] = row * wpr;
-        rg[0][r] = row * gpr;
+        rg[0][r] = m.scale_t ? row : row * gpr;
     }
     float acc[1][4] = {{0, 0, 0, 0}};
-    warp_qmm<BITS, GS, 1>(mats, rw, rg, row_ok, ng, xs, xsum, tstride, nt, acc);
+    warp_qmm<BITS, GS, 1>(mats, rw, rg, m.scale_t ? (size_t)m.rows : 1, row_ok, ng, xs, xsum, tstride, nt, acc);
 #pragma unroll
     for (int r = 0; r < 2; r++)
 #pragma unroll

@@ -12,6 +12,7 @@ struct QeQDev {
     const uint16_t *scales;
     const uint16_t *biases;
     int rows, cols, bits, group_size;
+    int scale_t;   /* 0: MLX layout [n][rows][groups]; 1: expert kernels' layout [n][groups][rows] */
 };
 
 /* Routing: fp32 router logits for E experts plus one extra column (index E) holding the shared-expert
@@ -54,7 +55,9 @@ int qe_launch_qmatvec(const QeQDev *m, const float *x, int T, float *y, cudaStre
 
 /* Synthetic weights generated in HBM (csrc/synth.h). */
 int qe_launch_synth_qmat(uint64_t seed, uint32_t block, uint32_t stream, int n, int rows, int cols, int bits,
-                         int gs, uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s);
+                         int gs, int scale_t, uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s);
+/* [n][rows][groups] -> [n][groups][rows] for a bf16 scale or bias tensor */
+int qe_launch_transpose_groups(const uint16_t *src, uint16_t *dst, int n, int rows, int groups, cudaStream_t s);
 int qe_launch_synth_normal(uint64_t seed, uint32_t block, uint32_t stream, size_t n, float sigma_c, float *out,
                            cudaStream_t s);
 

@@ -238,6 +238,7 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
         p.dst->scales = (const uint16_t *)(base + off); off += align256(gb);
         p.dst->biases = (const uint16_t *)(base + off); off += align256(gb);
         p.dst->rows = p.rows; p.dst->cols = p.cols; p.dst->bits = p.bits; p.dst->group_size = gs;
+        p.dst->scale_t = (&p - parts) < 6;   /* expert tensors keep scales/biases as [n][groups][rows] */
     }
     if (c->router_mode == QE_ROUTER_F32) {
         m->router_w = (float *)(base + off); off += align256(sizeof(float) * (size_t)(E + 1) * H);
@@ -267,24 +268,55 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
 
 int upload_q(const QeQDev *dst, const QeQTensor *src, int n, cudaStream_t s) {
     if (!src->w || !src->scales || !src->biases) QE_FAIL("missing quantized tensor");
+    const int ng = dst->cols / dst->group_size;
     const size_t wb = (size_t)n * dst->rows * ((size_t)dst->cols * dst->bits / 32) * 4;
-    const size_t gb = (size_t)n * dst->rows * ((size_t)dst->cols / dst->group_size) * 2;
+    const size_t gb = (size_t)n * dst->rows * (size_t)ng * 2;
     QE_CHECK(cudaMemcpyAsync((void *)dst->w, src->w, wb, cudaMemcpyHostToDevice, s));
-    QE_CHECK(cudaMemcpyAsync((void *)dst->scales, src->scales, gb, cudaMemcpyHostToDevice, s));
-    QE_CHECK(cudaMemcpyAsync((void *)dst->biases, src->biases, gb, cudaMemcpyHostToDevice, s));
+    if (!dst->scale_t) {
+        QE_CHECK(cudaMemcpyAsync((void *)dst->scales, src->scales, gb, cudaMemcpyHostToDevice, s));
+        QE_CHECK(cudaMemcpyAsync((void *)dst->biases, src->biases, gb, cudaMemcpyHostToDevice, s));
+        return 0;
+    }
+    /* MLX [n][rows][groups] in, [n][groups][rows] resident: a reversible transpose on the device */
+    uint16_t *tmp = nullptr;
+    QE_CHECK(cudaMalloc((void **)&tmp, gb));
+    int rc = cudaMemcpyAsync(tmp, src->scales, gb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+             qe_launch_transpose_groups(tmp, (uint16_t *)dst->scales, n, dst->rows, ng, s) ||
+             cudaMemcpyAsync(tmp, src->biases, gb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+             qe_launch_transpose_groups(tmp, (uint16_t *)dst->biases, n, dst->rows, ng, s) ||
+             cudaStreamSynchronize(s) != cudaSuccess;
+    cudaFree(tmp);
+    if (rc) QE_FAIL("scale upload failed");
     return 0;
 }
 
+/* Scale/bias i is generated from its MLX-order index (n, row, group) so the values match the CPU
+ * checker's copy; with scale_t it is stored at [n][group][row]. */
 __global__ void synth_qmat_kernel(uint64_t seed, uint32_t block, uint32_t stream, size_t nwords, size_t ngroups,
-                                  float scale_c, float neg_half, uint32_t *w, uint16_t *sc, uint16_t *bi) {
+                                  int rows, int ng, int scale_t, float scale_c, float neg_half, uint32_t *w,
+                                  uint16_t *sc, uint16_t *bi) {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nwords; i += stride)
         w[i] = syn_code_word(seed, block, stream, i);
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < ngroups; i += stride) {
         uint16_t s, b;
         syn_scale_bias(seed, block, stream, i, scale_c, neg_half, &s, &b);
-        sc[i] = s;
-        bi[i] = b;
+        size_t o = i;
+        if (scale_t) {
+            const size_t e = i / ((size_t)rows * ng), r = (i / ng) % rows, g = i % ng;
+            o = (e * ng + g) * rows + r;
+        }
+        sc[o] = s;
+        bi[o] = b;
+    }
+}
+
+__global__ void transpose_groups_kernel(const uint16_t *__restrict__ src, uint16_t *__restrict__ dst, int rows,
+                                        int ng, size_t total) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const size_t e = i / ((size_t)rows * ng), r = (i / ng) % rows, g = i % ng;
+        dst[(e * ng + g) * rows + r] = src[i];
     }
 }
 
@@ -307,10 +339,16 @@ __global__ void ops_kernel(int op, const float *__restrict__ a, const float *__r
 }  // namespace
 
 int qe_launch_synth_qmat(uint64_t seed, uint32_t block, uint32_t stream, int n, int rows, int cols, int bits, int gs,
-                         uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s) {
+                         int scale_t, uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s) {
     const size_t nwords = (size_t)n * rows * ((size_t)cols * bits / 32), ngroups = (size_t)n * rows * (cols / gs);
-    synth_qmat_kernel<<<1184, 256, 0, s>>>(seed, block, stream, nwords, ngroups, syn_scale_c(bits),
-                                           syn_neg_half_range(bits), w, sc, bi);
+    synth_qmat_kernel<<<1184, 256, 0, s>>>(seed, block, stream, nwords, ngroups, rows, cols / gs, scale_t,
+                                           syn_scale_c(bits), syn_neg_half_range(bits), w, sc, bi);
+    QE_CHECK(cudaGetLastError());
+    return 0;
+}
+
+int qe_launch_transpose_groups(const uint16_t *src, uint16_t *dst, int n, int rows, int groups, cudaStream_t s) {
+    transpose_groups_kernel<<<592, 256, 0, s>>>(src, dst, rows, groups, (size_t)n * rows * groups);
     QE_CHECK(cudaGetLastError());
     return 0;
 }
@@ -373,7 +411,7 @@ QeMoe *qe_moe_create_synthetic(const QeMoeConfig *cfg, uint64_t seed, uint32_t b
     cudaStream_t s = g_dev[m->device].stream;
     const int E = cfg->E, H = cfg->hidden, I = cfg->inter, Is = cfg->sh_inter, b = cfg->bits, gs = cfg->group_size;
     auto gen = [&](const QeQDev &q, uint32_t stream, int n) {
-        return qe_launch_synth_qmat(seed, block, stream, n, q.rows, q.cols, q.bits, gs, (uint32_t *)q.w,
+        return qe_launch_synth_qmat(seed, block, stream, n, q.rows, q.cols, q.bits, gs, q.scale_t, (uint32_t *)q.w,
                                     (uint16_t *)q.scales, (uint16_t *)q.biases, s);
     };
     int rc = gen(m->ex.gate, SYN_GATE, E) || gen(m->ex.up, SYN_UP, E) || gen(m->ex.down, SYN_DOWN, E) ||
@@ -603,7 +641,7 @@ int qe_qmat_matvec(const uint32_t *w, const uint16_t *scales, const uint16_t *bi
     q.biases = (const uint16_t *)(buf + align256(wb) + align256(gb));
     float *dx = (float *)(buf + align256(wb) + 2 * align256(gb));
     float *dy = (float *)((char *)dx + align256(4 * (size_t)cols));
-    q.rows = rows; q.cols = cols; q.bits = bits; q.group_size = group_size;
+    q.rows = rows; q.cols = cols; q.bits = bits; q.group_size = group_size; q.scale_t = 0;
     int rc = cudaMemcpyAsync((void *)q.w, w, wb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
              cudaMemcpyAsync((void *)q.scales, scales, gb, cudaMemcpyHostToDevice, s) != cudaSuccess ||
              cudaMemcpyAsync((void *)q.biases, biases, gb, cudaMemcpyHostToDevice, s) != cudaSuccess ||

@@ -74,56 +74,89 @@ __global__ void __launch_bounds__(128) router_gemv_f32_kernel(const float *__res
     }
 }
 
-/* Prefill: 64 rows x 32 tokens per CTA, 256 threads, 4 rows x 2 tokens per thread. The K loop runs in
- * 64-input chunks; within a chunk every accumulator is an fmaf chain in ascending k, and at the end of
- * the chunk it is added to the running total, which is exactly or_dot_f32's order. */
+/* Prefill: 64 router rows x 32 tokens per CTA, 128 threads, 4 rows x 4 tokens per thread. The K loop runs
+ * in 64-input chunks; within a chunk every accumulator is an fmaf chain in ascending k, and at the end of
+ * the chunk it is added to the running total: exactly or_dot_f32's order. Chunks are double-buffered in
+ * shared memory, stored k-major ([k][row], [k][token]) so each k step is two broadcast 16-byte loads. */
 constexpr int kGR = 64, kGT = 32;
-__global__ void __launch_bounds__(256) router_gemm_f32_kernel(const float *__restrict__ W,
+__global__ void __launch_bounds__(128) router_gemm_f32_kernel(const float *__restrict__ W,
                                                               const float *__restrict__ bias,
                                                               const float *__restrict__ x, int T, int H, int E,
                                                               float *__restrict__ logits) {
-    __shared__ __align__(16) float Ws[kChunk][kGR];   /* [k][row] */
-    __shared__ __align__(16) float Xs[kChunk][kGT];   /* [k][token] */
-    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    __shared__ __align__(16) float Ws[2][kChunk][kGR];   /* [buf][k][row]   */
+    __shared__ __align__(16) float Xs[2][kChunk][kGT];   /* [buf][k][token] */
+    const int tid = threadIdx.x, tx = tid & 7, ty = tid >> 3;
     const int r0 = blockIdx.x * kGR, t0 = blockIdx.y * kGT;
     const int Ep1 = E + 1;
-    float total[4][2], acc[4][2];
+    const int nch = (H + kChunk - 1) / kChunk;
+    /* loader mapping: W row = tid & 63, k quads (tid >> 6) + 2i (i < 8); X token = tid & 31, k quads
+     * (tid >> 5) + 4i (i < 4). Consecutive lanes -> consecutive rows/tokens: conflict-free stores. */
+    const int lr = tid & 63, lkq = tid >> 6, xr = tid & 31, xkq = tid >> 5;
+    const bool wrow_ok = r0 + lr < Ep1, xrow_ok = t0 + xr < T;
+    const float *wsrc = W + (size_t)(wrow_ok ? r0 + lr : 0) * H;
+    const float *xsrc = x + (size_t)(xrow_ok ? t0 + xr : 0) * H;
+    float4 wreg[8], xreg[4];
+    auto load = [&](int c) {
+        const int k0 = c * kChunk;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int k = k0 + 4 * (lkq + 2 * i);
+            wreg[i] = (wrow_ok && k + 3 < H) ? __ldg(reinterpret_cast<const float4 *>(wsrc + k))
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int k = k0 + 4 * (xkq + 4 * i);
+            xreg[i] = (xrow_ok && k + 3 < H) ? __ldg(reinterpret_cast<const float4 *>(xsrc + k))
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store = [&](int b) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int k = 4 * (lkq + 2 * i);
+            Ws[b][k][lr] = wreg[i].x; Ws[b][k + 1][lr] = wreg[i].y;
+            Ws[b][k + 2][lr] = wreg[i].z; Ws[b][k + 3][lr] = wreg[i].w;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int k = 4 * (xkq + 4 * i);
+            Xs[b][k][xr] = xreg[i].x; Xs[b][k + 1][xr] = xreg[i].y;
+            Xs[b][k + 2][xr] = xreg[i].z; Xs[b][k + 3][xr] = xreg[i].w;
+        }
+    };
+    float total[4][4], acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int j = 0; j < 2; j++) total[i][j] = 0.0f;
-    for (int k0 = 0; k0 < H; k0 += kChunk) {
-        const int kn = min(kChunk, H - k0);
-        /* W tile: 64 rows x 64 k, transposed into Ws[k][row] */
-        for (int e = tid; e < kGR * kChunk; e += 256) {
-            const int r = e / kChunk, k = e % kChunk;
-            const int gr = r0 + r;
-            Ws[k][r] = (gr < Ep1 && k < kn) ? __ldg(W + (size_t)gr * H + k0 + k) : 0.0f;
-        }
-        for (int e = tid; e < kGT * kChunk; e += 256) {
-            const int t = e / kChunk, k = e % kChunk;
-            const int gt = t0 + t;
-            Xs[k][t] = (gt < T && k < kn) ? __ldg(x + (size_t)gt * H + k0 + k) : 0.0f;
-        }
-        __syncthreads();
+        for (int j = 0; j < 4; j++) total[i][j] = 0.0f;
+    load(0);
+    store(0);
+    __syncthreads();
+    for (int c = 0; c < nch; c++) {
+        const int b = c & 1;
+        if (c + 1 < nch) load(c + 1);
+        const int kn = min(kChunk, H - c * kChunk);
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 2; j++) acc[i][j] = 0.0f;
+            for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+#pragma unroll 8
         for (int k = 0; k < kn; k++) {
-            const float4 wv = *reinterpret_cast<const float4 *>(&Ws[k][ty * 4]);
-            const float2 xv = *reinterpret_cast<const float2 *>(&Xs[k][tx * 2]);
+            const float4 wv = *reinterpret_cast<const float4 *>(&Ws[b][k][ty * 4]);
+            const float4 xv = *reinterpret_cast<const float4 *>(&Xs[b][k][tx * 4]);
             const float wr[4] = {wv.x, wv.y, wv.z, wv.w};
-            const float xr[2] = {xv.x, xv.y};
+            const float xr4[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 2; j++) acc[i][j] = __fmaf_rn(wr[i], xr[j], acc[i][j]);
+                for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(wr[i], xr4[j], acc[i][j]);
         }
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 2; j++) total[i][j] = __fadd_rn(total[i][j], acc[i][j]);
+            for (int j = 0; j < 4; j++) total[i][j] = __fadd_rn(total[i][j], acc[i][j]);
+        if (c + 1 < nch) store(b ^ 1);
         __syncthreads();
     }
 #pragma unroll
@@ -131,8 +164,8 @@ __global__ void __launch_bounds__(256) router_gemm_f32_kernel(const float *__res
         const int r = r0 + ty * 4 + i;
         if (r >= Ep1) continue;
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const int t = t0 + tx * 2 + j;
+        for (int j = 0; j < 4; j++) {
+            const int t = t0 + tx * 4 + j;
             if (t >= T) continue;
             float l = total[i][j];
             if (bias && r < E) l = __fadd_rn(l, bias[r]);
@@ -360,8 +393,9 @@ int qe_launch_router_f32(const float *W, const float *bias, const float *x, int 
         router_gemv_f32_kernel<<<(rows + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, s>>>(
             W, bias, x, T, H, E, logits);
     } else {
+        if (H % 4) QE_FAIL("router: hidden %d must be a multiple of 4", H);
         dim3 grid((E + 1 + kGR - 1) / kGR, (T + kGT - 1) / kGT);
-        router_gemm_f32_kernel<<<grid, 256, 0, s>>>(W, bias, x, T, H, E, logits);
+        router_gemm_f32_kernel<<<grid, 128, 0, s>>>(W, bias, x, T, H, E, logits);
     }
     QE_CHECK(cudaGetLastError());
     return 0;

@@ -28,35 +28,43 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
+/* try_wait with a suspend hint: the thread sleeps in hardware until the phase completes (or the hint,
+ * in ns, elapses), so waiting warps do not spin on the issue slots. */
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(1000000u)
         : "memory");
     return ok != 0;
 }
 
 /* Wait for phase `parity` of an mbarrier, for at most QE_WAIT_NS. Returns false (and raises *abort,
- * records `code` in *err) on timeout or when another thread already aborted. */
+ * records `code` in *err when err is non-null) on timeout or when another thread already aborted. */
 #define QE_WAIT_NS 2000000000ull
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort, int *err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
-    for (uint32_t i = 0;; i++) {
+    while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 63u) == 0) {
-            if (*abort) return false;
-            if (global_timer_ns() - t0 > QE_WAIT_NS) {
-                *abort = 1;
-                if (err) atomicCAS(err, 0, code);
-                return false;
-            }
+        if (*abort) return false;
+        if (global_timer_ns() - t0 > QE_WAIT_NS) {
+            *abort = 1;
+            if (err) atomicCAS(err, 0, code);
+            return false;
         }
     }
+}
+
+/* 16-byte global -> shared async copy (L2 only), and an mbarrier arrival when this thread's copies land. */
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 /* TMA tile loads (no multicast), completion counted on an mbarrier. */

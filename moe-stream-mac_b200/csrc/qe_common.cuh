@@ -82,6 +82,12 @@ __device__ __forceinline__ float qe_silu_mul(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, qe_expf(-g))), u);
 }
 
+/* Same formula with CUDA's expf: for the SwiGLU inside the expert kernels, whose results are compared
+ * within tolerance (routing, which must be bit-exact, always uses qe_expf). */
+__device__ __forceinline__ float qe_silu_mul_fast(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
 /* 1 / (1 + expf(-x)), engine/src/ops.c:23-27. */
 __device__ __forceinline__ float qe_sigmoid(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, qe_expf(-x))); }
 

@@ -105,6 +105,20 @@ int qe_op_sigmoid(float *out, const float *x, int n);
 /* The device expf used by softmax, on n inputs (for comparison with the host C library's expf). */
 int qe_op_expf(float *out, const float *x, int n);
 
+/* Routing (fp32 router, softmax, top-k, renormalisation) on device buffers without allocating any device
+ * memory. No counterpart in the reference. It is for callers that cannot let a library call cudaMalloc:
+ * a framework whose caching allocator already owns the device memory, or a decode loop that cannot take
+ * the device-wide synchronisation an allocation may cause. router_w: device [E+1][hidden] fp32 (rows
+ * 0..E-1 the router, row E the shared-expert gate vector, as qe_moe_create stores them); router_bias: device
+ * [E] or NULL; x: device [T][hidden]; idx/score: device [T][top_k]; stream: a cudaStream_t (NULL = legacy
+ * default). The only scratch, the logits, lives in a fixed 4 MiB device array (2^20 floats) that every GPU
+ * loading the library holds until exit: T*(E+1) must not exceed 2^20 (T <= 4080 at E = 256), larger T is
+ * refused with -1. All calls share that array, so calls that overlap on the GPU race. The first call on a
+ * device looks up the array's device address, so make it before any stream capture. Same results as
+ * qe_moe_route for the same weights. 0 ok, -1 error (message on stderr). */
+int qe_route_f32_noalloc(const float *router_w, const float *router_bias, const float *x, int T, int hidden, int E,
+                         int top_k, int32_t *idx, float *score, void *stream);
+
 /* ---- engine-level statistics (engine/include/qengine.h:20-23 counterparts) ---- */
 double qe_expert_gb_read(void);        /* GB of expert weights streamed from HBM by qe_moe_forward */
 double qe_expert_read_seconds(void);   /* GPU seconds spent in qe_moe_forward's kernels            */

@@ -69,6 +69,7 @@ def lib() -> C.CDLL:
         L.qe_profile_end.argtypes = [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         L.qe_kernel_launches.restype = C.c_ulonglong
         L.qe_device_error.restype = C.c_int
+        L.qe_route_f32_noalloc.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp]
         _lib = L
     return _lib
 

@@ -35,6 +35,9 @@ __device__ int warp_exclusive_scan(int *a, int n, int lane) {
     return __shfl_sync(QE_FULL, incl, 31);
 }
 
+/* two compact arrays of E+2 ints after the six per-expert arrays */
+__device__ __forceinline__ int *cnt_tmp(int *sm, int E) { return sm + 6 * (E + 2); }
+
 __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restrict__ idx, int T, int E, int k,
                                                           int tiles_gu, int tiles_sh_gu, int tiles_dn, int chunk,
                                                           QeBuckets b) {
@@ -73,38 +76,37 @@ __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restr
         if (lane == 0) flag[E + 1] = na;
     }
     __syncthreads();
-    /* compact the per-slot item counts into active-slot order, then scan them */
+    /* active slots in expert order: slot_expert[a] = e; their work-item counts, compacted and scanned in
+     * shared memory (igu/idn are reused as the compact arrays: entry a <= e, written after a barrier) */
+    int *cgu = cnt_tmp(sm, E);                  /* [E+2] compact gate/up item counts */
+    int *cdn = cgu + (E + 2);                   /* [E+2] compact down item counts   */
     for (int e = tid; e <= E; e += kThreads) {
         cur[e] = off[e];
         if (cnt[e] > 0) {
             const int a = flag[e];
             b.slot_expert[a] = e;
+            cgu[a] = igu[e];
+            cdn[a] = idn[e];
         }
     }
     __syncthreads();
     const int na = flag[E + 1];
-    /* reuse the tail of idn/igu as compact arrays: build compact lists in registers via the slot map */
-    for (int a = tid; a < na; a += kThreads) {
-        const int e = b.slot_expert[a];
-        b.slot_items[a] = igu[e];
-        b.slot_items[(E + 2) + a] = idn[e];
+    if (tid < 32) {
+        const int tot = warp_exclusive_scan(cgu, na, lane);
+        if (lane == 0) cgu[na] = tot;
+    } else if (tid < 64) {
+        const int tot = warp_exclusive_scan(cdn, na, lane);
+        if (lane == 0) cdn[na] = tot;
     }
     __syncthreads();
-    __threadfence_block();
+    for (int a = tid; a <= na; a += kThreads) {
+        b.slot_items[a] = cgu[a];
+        b.slot_items[(E + 2) + a] = cdn[a];
+    }
     if (tid == 0) {
-        int sg = 0, sd = 0;
-        for (int a = 0; a < na; a++) {
-            const int vg = b.slot_items[a], vd = b.slot_items[(E + 2) + a];
-            b.slot_items[a] = sg;
-            b.slot_items[(E + 2) + a] = sd;
-            sg += vg;
-            sd += vd;
-        }
-        b.slot_items[na] = sg;
-        b.slot_items[(E + 2) + na] = sd;
         b.n_active[0] = na;
-        b.n_active[1] = sg;
-        b.n_active[2] = sd;
+        b.n_active[1] = cgu[na];
+        b.n_active[2] = cdn[na];
     }
     /* scatter the pairs into their buckets */
     for (int q = tid; q < npairs; q += kThreads) {
@@ -126,7 +128,7 @@ __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restr
 
 int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int tiles_gu, int tiles_sh_gu, int tiles_dn,
                      int chunk, const QeBuckets *b, cudaStream_t s) {
-    const size_t smem = sizeof(int) * (size_t)(6 * (E + 2));
+    const size_t smem = sizeof(int) * (size_t)(8 * (E + 2));
     bucket_kernel<<<1, kThreads, smem, s>>>(idx, T, E, k, tiles_gu, tiles_sh_gu, tiles_dn, chunk, *b);
     QE_CHECK(cudaGetLastError());
     return 0;

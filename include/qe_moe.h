@@ -39,6 +39,9 @@ typedef struct {
     int max_tokens;       /* tokens per internal pass (scratch sizing); forward accepts any T >= 1 */
     int device;           /* CUDA device ordinal */
     int layer;            /* layer id written to the QE_TRACE routing trace (moe_layer.c:57-64) */
+    int ep_rank, ep_size; /* expert parallelism: this handle holds routed experts [ep_rank*E/ep_size,
+                             (ep_rank+1)*E/ep_size) plus the router and the shared expert (replicated).
+                             ep_size 0 or 1 = all experts (then ep_rank must be 0). ep_size must divide E. */
 } QeMoeConfig;
 
 /* One quantized tensor in the MLX affine layout (engine/include/qmat.h:3-11): uint32 codes
@@ -71,7 +74,8 @@ QeMoe *qe_moe_create_synthetic(const QeMoeConfig *cfg, uint64_t seed, uint32_t b
 void qe_moe_free(QeMoe *m);
 
 /* out[T][hidden] = moe(x[T][hidden]) for T >= 1 independent tokens, host buffers (x, out may not alias).
- * Replaces T calls of moe_layer_step (engine/src/moe_layer.c:66-89). 0 ok, -1 error (out untouched). */
+ * Replaces T calls of moe_layer_step (engine/src/moe_layer.c:66-89). 0 ok, -1 error (out untouched).
+ * A handle holding a subset of the experts (ep_size > 1) refuses it: use the qe_moe_ep_* calls. */
 int qe_moe_forward(QeMoe *m, int T, const float *x, float *out);
 
 /* Same on device buffers of m's device, enqueued on `stream` (a cudaStream_t, NULL = legacy default),
@@ -81,6 +85,34 @@ int qe_moe_forward_device(QeMoe *m, int T, const float *x, float *out, void *str
 /* Routing only (moe_layer.c:29-37): idx[T][top_k] expert ids, score[T][top_k] renormalised weights,
  * host buffers. */
 int qe_moe_route(QeMoe *m, int T, const float *x, int32_t *idx, float *score);
+
+/* ---- expert parallelism (one process and one handle per GPU; the caller runs the collectives) ----
+ * No counterpart in the reference (single-process, engine/src/moe_layer.c). Experts are sharded by id:
+ * expert e lives on rank e / (E/ep_size). All buffers are device buffers on the handle's device, enqueued
+ * on `stream` (a cudaStream_t). A token's slot list "meta" is int32 [2*top_k]: the k global expert ids
+ * (-1 = empty slot) followed by the k renormalised scores' float bits.
+ *
+ * Token-sharded step (prefill batches, C4/C5 style), per rank with its own T tokens, G = ep_size:
+ *   qe_moe_ep_route_device    route x, write meta[T][2k], and the gated shared-expert term shared[T][h]
+ *   qe_moe_ep_pack_device     send_x[G][T][h], send_meta[G][T][2k]: rows of the tokens with >= 1 expert on
+ *                             rank d go to block d in token order, the rest of the block is padding (meta ids
+ *                             -1); home[G][T] = a token's row in block d or -1; counts[G] rows per block
+ *   (caller) all_to_all of send_x and send_meta in equal blocks of T rows
+ *   qe_moe_ep_experts_device  partial[n][h] for received rows: sum over the slots this rank owns, in slot
+ *                             order, of score * expert(x)  (rows without such slots give 0)
+ *   (caller) all_to_all of partial back to the home ranks
+ *   qe_moe_ep_combine_device  out[t] = (sum over d ascending of part[d][home[d][t]]) + shared[t]
+ * Replicated step (decode: every rank holds the same T tokens): route, experts on the own meta, an all-gather
+ * of the partials into part[G][T][h], combine with home = NULL (part[d][t]).
+ * With ep_size = 1 the token-sharded step gives results bit-identical to qe_moe_forward_device on the same
+ * expert path; with more ranks the fp32 sum is grouped by rank (within tolerance of the reference). */
+int qe_moe_ep_route_device(QeMoe *m, int T, const float *x, int32_t *meta, float *shared, void *stream);
+int qe_moe_ep_pack_device(QeMoe *m, int T, const float *x, const int32_t *meta, float *send_x, int32_t *send_meta,
+                          int32_t *home, int32_t *counts, void *stream);
+int qe_moe_ep_experts_device(QeMoe *m, int n, const float *x, const int32_t *meta, float *partial, void *stream);
+int qe_moe_ep_combine_device(QeMoe *m, int T, const float *part, const int32_t *home, const float *shared, float *out,
+                             void *stream);
+int qe_moe_ep_size(const QeMoe *m);
 
 /* Block accessors. */
 int qe_moe_hidden(const QeMoe *m);

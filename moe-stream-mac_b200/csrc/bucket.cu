@@ -3,7 +3,8 @@
  * Replaces the reference's per-token expert loop (engine/src/moe_layer.c:79-83, prefill = T calls) and
  * the batched template of its MLX path (engine/hybrid/hybrid.py:177-189: unique experts + inverse index,
  * tokens sorted by expert) with a histogram + prefix scan + scatter on the GPU. Every (token, slot) pair
- * p = t*(k+1) + j (j = k is the shared expert) lands in its expert's bucket; the active buckets and the
+ * p = t*(k+1) + j (j = k is the shared expert) lands in its expert's bucket (slots whose expert id is outside
+ * [0, E) are skipped: the experts another GPU owns); the active buckets and the
  * work items of the gate/up and down kernels are listed so those kernels run a compact grid.
  * Numerics do not depend on the order of pairs inside a bucket (every pair is an independent MMA column).
  */
@@ -39,8 +40,8 @@ __device__ int warp_exclusive_scan(int *a, int n, int lane) {
 __device__ __forceinline__ int *cnt_tmp(int *sm, int E) { return sm + 6 * (E + 2); }
 
 __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restrict__ idx, int T, int E, int k,
-                                                          int tiles_gu, int tiles_sh_gu, int tiles_dn, int chunk,
-                                                          QeBuckets b) {
+                                                          int shared_tokens, int tiles_gu, int tiles_sh_gu,
+                                                          int tiles_dn, int chunk, QeBuckets b) {
     extern __shared__ int sm[];
     int *cnt = sm;                 /* [E+1] */
     int *off = cnt + (E + 1);      /* [E+2] */
@@ -57,7 +58,7 @@ __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restr
         if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    if (tid == 0) cnt[E] = T;
+    if (tid == 0) cnt[E] = shared_tokens;   /* T, or 0 when the shared expert is computed elsewhere */
     __syncthreads();
     for (int e = tid; e <= E; e += kThreads) {
         off[e] = cnt[e];
@@ -116,7 +117,7 @@ __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restr
         const int pos = atomicAdd(&cur[e], 1);
         b.pairs[pos] = t * (k + 1) + j;
     }
-    for (int t = tid; t < T; t += kThreads) b.pairs[off[E] + t] = t * (k + 1) + k;
+    for (int t = tid; t < shared_tokens; t += kThreads) b.pairs[off[E] + t] = t * (k + 1) + k;
     for (int e = tid; e <= E; e += kThreads) {
         b.counts[e] = cnt[e];
         b.offsets[e] = off[e];
@@ -126,10 +127,10 @@ __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restr
 
 }  // namespace
 
-int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int tiles_gu, int tiles_sh_gu, int tiles_dn,
-                     int chunk, const QeBuckets *b, cudaStream_t s) {
+int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int shared_tokens, int tiles_gu, int tiles_sh_gu,
+                     int tiles_dn, int chunk, const QeBuckets *b, cudaStream_t s) {
     const size_t smem = sizeof(int) * (size_t)(8 * (E + 2));
-    bucket_kernel<<<1, kThreads, smem, s>>>(idx, T, E, k, tiles_gu, tiles_sh_gu, tiles_dn, chunk, *b);
+    bucket_kernel<<<1, kThreads, smem, s>>>(idx, T, E, k, shared_tokens, tiles_gu, tiles_sh_gu, tiles_dn, chunk, *b);
     QE_CHECK(cudaGetLastError());
     return 0;
 }

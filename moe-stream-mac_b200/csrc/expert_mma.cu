@@ -366,6 +366,23 @@ __global__ void combine_kernel(const float *__restrict__ ybuf, const float *__re
     out[i] = o;
 }
 
+/* Expert-parallel partial sums (moe_layer.c:79-88 split by owner GPU): out[t] = sum over the routed slots
+ * this GPU owns (idx >= 0), in slot order, of score * y, and/or sigmoid(gsh) * y_shared. */
+__global__ void combine_sel_kernel(const float *__restrict__ ybuf, const int32_t *__restrict__ idx,
+                                   const float *__restrict__ score, const float *__restrict__ logits, int ld_logits,
+                                   int T, int E, int k, int H, int with_routed, int with_shared,
+                                   float *__restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)T * H) return;
+    const int t = (int)(i / H), j = (int)(i % H);
+    const float *y = ybuf + (size_t)t * (k + 1) * H + j;
+    float o = 0.0f;
+    if (with_routed)
+        for (int s = 0; s < k; s++)
+            if (idx[(size_t)t * k + s] >= 0) o = __fadd_rn(o, __fmul_rn(score[(size_t)t * k + s], y[(size_t)s * H]));
+    if (with_shared) o = __fadd_rn(o, __fmul_rn(qe_sigmoid(logits[(size_t)t * ld_logits + E]), y[(size_t)k * H]));
+    out[i] = o;
+}
 
 /* y[t][rows] = W x_t for T vectors (qmat_matvec semantics, engine/src/qmat.c:15-49): CTA = 64 rows x
  * 8 vectors, same warp routine as the expert kernels. */
@@ -438,6 +455,16 @@ int qe_launch_combine(const float *ybuf, const float *score, const float *logits
                       int H, float *out, cudaStream_t s) {
     const long long n = (long long)T * H;
     combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ybuf, score, logits, ld_logits, T, E, k, H, out);
+    QE_CHECK(cudaGetLastError());
+    return 0;
+}
+
+int qe_launch_combine_sel(const float *ybuf, const int32_t *idx, const float *score, const float *logits,
+                          int ld_logits, int T, int E, int k, int H, int with_routed, int with_shared, float *out,
+                          cudaStream_t s) {
+    const long long n = (long long)T * H;
+    combine_sel_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ybuf, idx, score, logits, ld_logits, T, E, k, H,
+                                                                   with_routed, with_shared, out);
     QE_CHECK(cudaGetLastError());
     return 0;
 }

@@ -34,8 +34,8 @@ struct QeBuckets {
     int32_t *slot_items;  /* [2][E+2] per-slot work-item prefix, gate/up & down */
     int32_t *n_active;    /* [3]: active slots, gate/up items, down items     */
 };
-int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int tiles_gu, int tiles_sh_gu, int tiles_dn,
-                     int chunk, const QeBuckets *b, cudaStream_t s);
+int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int shared_tokens, int tiles_gu, int tiles_sh_gu,
+                     int tiles_dn, int chunk, const QeBuckets *b, cudaStream_t s);
 
 /* Expert kernels (mma.sync split-bf16 path). */
 struct QeExpertArgs {
@@ -49,13 +49,17 @@ int qe_launch_down(const QeExpertArgs *a, const float *h3, int ldh, const QeBuck
                    float *ybuf /*[T*(k+1)][H]*/, int grid, cudaStream_t s);
 int qe_launch_combine(const float *ybuf, const float *score, const float *logits, int ld_logits, int T, int E,
                       int k, int H, float *out, cudaStream_t s);
+/* Expert-parallel variants: the routed slots whose idx is >= 0 (slot order), and/or the gated shared expert. */
+int qe_launch_combine_sel(const float *ybuf, const int32_t *idx, const float *score, const float *logits,
+                          int ld_logits, int T, int E, int k, int H, int with_routed, int with_shared, float *out,
+                          cudaStream_t s);
 
 /* Generic quantized matrix-vector products (engine/src/qmat.c:15-49 semantics) over T vectors. */
 int qe_launch_qmatvec(const QeQDev *m, const float *x, int T, float *y, cudaStream_t s);
 
 /* Synthetic weights generated in HBM (csrc/synth.h). */
-int qe_launch_synth_qmat(uint64_t seed, uint32_t block, uint32_t stream, int n, int rows, int cols, int bits,
-                         int gs, int scale_t, uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s);
+int qe_launch_synth_qmat(uint64_t seed, uint32_t block, uint32_t stream, int first, int n, int rows, int cols,
+                         int bits, int gs, int scale_t, uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s);
 /* [n][rows][groups] -> [n][groups][rows] for a bf16 scale or bias tensor */
 int qe_launch_transpose_groups(const uint16_t *src, uint16_t *dst, int n, int rows, int groups, cudaStream_t s);
 int qe_launch_synth_normal(uint64_t seed, uint32_t block, uint32_t stream, size_t n, float sigma_c, float *out,

@@ -164,6 +164,7 @@ struct QeMoe {
     QeQDev router_q, sh_router_q;
     QeExpertArgs ex;
     size_t expert_bytes;    /* bytes of one routed expert (gate+up+down codes, scales, biases) */
+    int e0, E_loc;          /* routed experts held here: global ids [e0, e0 + E_loc) (expert parallelism) */
     int path;               /* 0 = auto, 1 = mma.sync only, 2 = tensor-core (tcgen05) whenever supported */
     bool tc;                /* tensor-core path available for this shape */
     alignas(64) unsigned char maps_gu[2 * 2 * 3 * 128];  /* [routed/shared][gate/up][codes, scales, biases] */
@@ -186,6 +187,10 @@ int validate(const QeMoeConfig *c) {
     if (c->router_mode != QE_ROUTER_F32 && c->router_mode != QE_ROUTER_QMAT) QE_FAIL("bad router_mode");
     if (c->router_mode == QE_ROUTER_QMAT && c->router_bits != 4 && c->router_bits != 8)
         QE_FAIL("router_bits=%d: only 4 and 8", c->router_bits);
+    const int G = c->ep_size < 1 ? 1 : c->ep_size;
+    if (G > 64 || c->E % G) QE_FAIL("ep_size=%d must divide E=%d (at most 64)", c->ep_size, c->E);
+    if (c->ep_rank < 0 || c->ep_rank >= G) QE_FAIL("ep_rank=%d outside [0, %d)", c->ep_rank, G);
+    if (c->E / G < 1) QE_FAIL("no experts per rank");
     return 0;
 }
 
@@ -205,11 +210,15 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     memset(m, 0, sizeof(QeMoe));
     m->cfg = *c;
     if (m->cfg.max_tokens < 1) m->cfg.max_tokens = 4096;
+    if (m->cfg.ep_size < 1) m->cfg.ep_size = 1;
     m->device = c->device;
-    const int E = c->E, H = c->hidden, I = c->inter, Is = c->sh_inter, b = c->bits, gs = c->group_size;
+    m->E_loc = c->E / m->cfg.ep_size;
+    m->e0 = m->cfg.ep_rank * m->E_loc;
+    const int E = c->E, El = m->E_loc, H = c->hidden, I = c->inter, Is = c->sh_inter, b = c->bits,
+              gs = c->group_size;
     struct Part { int n, rows, cols, bits; QeQDev *dst; };
     Part parts[8] = {
-        {E, I, H, b, &m->ex.gate}, {E, I, H, b, &m->ex.up}, {E, H, I, b, &m->ex.down},
+        {El, I, H, b, &m->ex.gate}, {El, I, H, b, &m->ex.up}, {El, H, I, b, &m->ex.down},
         {1, Is, H, b, &m->ex.sh_gate}, {1, Is, H, b, &m->ex.sh_up}, {1, H, Is, b, &m->ex.sh_down},
         {c->router_mode == QE_ROUTER_QMAT ? 1 : 0, E, H, c->router_bits, &m->router_q},
         {c->router_mode == QE_ROUTER_QMAT ? 1 : 0, 1, H, c->router_bits, &m->sh_router_q}};
@@ -244,7 +253,7 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
         m->router_w = (float *)(base + off); off += align256(sizeof(float) * (size_t)(E + 1) * H);
         m->router_bias = (float *)(base + off); off += align256(4 * (size_t)E);
     }
-    m->ex.E = E; m->ex.k = c->top_k; m->ex.hidden = H; m->ex.inter = I; m->ex.sh_inter = Is;
+    m->ex.E = El; m->ex.k = c->top_k; m->ex.hidden = H; m->ex.inter = I; m->ex.sh_inter = Is;
     size_t wb, gb;
     m->expert_bytes = qbytes(1, I, H, b, gs, &wb, &gb) * 2 + qbytes(1, H, I, b, gs, &wb, &gb);
     const char *path = getenv("QE_EXPERT_PATH");   /* auto (default) | mma | tc */
@@ -257,18 +266,23 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
         for (int r = 0; r < 2 && m->tc; r++) {
             for (int q = 0; q < 2 && m->tc; q++) {
                 unsigned char *o = m->maps_gu + ((r * 2 + q) * 3) * mb;
-                m->tc = !qe_tc_weight_maps(gu[r][q], r ? 1 : E, o, o + mb, o + 2 * mb);
+                m->tc = !qe_tc_weight_maps(gu[r][q], r ? 1 : El, o, o + mb, o + 2 * mb);
             }
             unsigned char *o = m->maps_dn + (r * 3) * mb;
-            if (m->tc) m->tc = !qe_tc_weight_maps(dn[r], r ? 1 : E, o, o + mb, o + 2 * mb);
+            if (m->tc) m->tc = !qe_tc_weight_maps(dn[r], r ? 1 : El, o, o + mb, o + 2 * mb);
         }
     }
     return m;
 }
 
-int upload_q(const QeQDev *dst, const QeQTensor *src, int n, cudaStream_t s) {
-    if (!src->w || !src->scales || !src->biases) QE_FAIL("missing quantized tensor");
+/* Copies matrices [first, first + n) of a host tensor into dst. */
+int upload_q(const QeQDev *dst, const QeQTensor *src0, int n, cudaStream_t s, int first = 0) {
+    if (!src0->w || !src0->scales || !src0->biases) QE_FAIL("missing quantized tensor");
     const int ng = dst->cols / dst->group_size;
+    const size_t wpm = (size_t)dst->rows * ((size_t)dst->cols * dst->bits / 32), gpm = (size_t)dst->rows * ng;
+    QeQTensor src1 = {src0->w + (size_t)first * wpm, src0->scales + (size_t)first * gpm,
+                      src0->biases + (size_t)first * gpm};
+    const QeQTensor *src = &src1;
     const size_t wb = (size_t)n * dst->rows * ((size_t)dst->cols * dst->bits / 32) * 4;
     const size_t gb = (size_t)n * dst->rows * (size_t)ng * 2;
     QE_CHECK(cudaMemcpyAsync((void *)dst->w, src->w, wb, cudaMemcpyHostToDevice, s));
@@ -291,16 +305,17 @@ int upload_q(const QeQDev *dst, const QeQTensor *src, int n, cudaStream_t s) {
 }
 
 /* Scale/bias i is generated from its MLX-order index (n, row, group) so the values match the CPU
- * checker's copy; with scale_t it is stored at [n][group][row]. */
-__global__ void synth_qmat_kernel(uint64_t seed, uint32_t block, uint32_t stream, size_t nwords, size_t ngroups,
-                                  int rows, int ng, int scale_t, float scale_c, float neg_half, uint32_t *w,
-                                  uint16_t *sc, uint16_t *bi) {
+ * checker's copy; with scale_t it is stored at [n][group][row]. word0/group0: index of the first generated
+ * element in the whole tensor (an expert-parallel handle generates only its own experts' slice). */
+__global__ void synth_qmat_kernel(uint64_t seed, uint32_t block, uint32_t stream, size_t word0, size_t group0,
+                                  size_t nwords, size_t ngroups, int rows, int ng, int scale_t, float scale_c,
+                                  float neg_half, uint32_t *w, uint16_t *sc, uint16_t *bi) {
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nwords; i += stride)
-        w[i] = syn_code_word(seed, block, stream, i);
+        w[i] = syn_code_word(seed, block, stream, word0 + i);
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < ngroups; i += stride) {
         uint16_t s, b;
-        syn_scale_bias(seed, block, stream, i, scale_c, neg_half, &s, &b);
+        syn_scale_bias(seed, block, stream, group0 + i, scale_c, neg_half, &s, &b);
         size_t o = i;
         if (scale_t) {
             const size_t e = i / ((size_t)rows * ng), r = (i / ng) % rows, g = i % ng;
@@ -338,10 +353,11 @@ __global__ void ops_kernel(int op, const float *__restrict__ a, const float *__r
 
 }  // namespace
 
-int qe_launch_synth_qmat(uint64_t seed, uint32_t block, uint32_t stream, int n, int rows, int cols, int bits, int gs,
-                         int scale_t, uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s) {
-    const size_t nwords = (size_t)n * rows * ((size_t)cols * bits / 32), ngroups = (size_t)n * rows * (cols / gs);
-    synth_qmat_kernel<<<1184, 256, 0, s>>>(seed, block, stream, nwords, ngroups, rows, cols / gs, scale_t,
+int qe_launch_synth_qmat(uint64_t seed, uint32_t block, uint32_t stream, int first, int n, int rows, int cols,
+                         int bits, int gs, int scale_t, uint32_t *w, uint16_t *sc, uint16_t *bi, cudaStream_t s) {
+    const size_t wpm = (size_t)rows * ((size_t)cols * bits / 32), gpm = (size_t)rows * (cols / gs);
+    synth_qmat_kernel<<<1184, 256, 0, s>>>(seed, block, stream, (size_t)first * wpm, (size_t)first * gpm,
+                                           (size_t)n * wpm, (size_t)n * gpm, rows, cols / gs, scale_t,
                                            syn_scale_c(bits), syn_neg_half_range(bits), w, sc, bi);
     QE_CHECK(cudaGetLastError());
     return 0;
@@ -376,8 +392,9 @@ QeMoe *qe_moe_create(const QeMoeConfig *cfg, const QeMoeWeights *w) {
     if (!m) return nullptr;
     DevCtx *d = &g_dev[m->device];
     cudaStream_t s = d->stream;
-    int rc = upload_q(&m->ex.gate, &w->gate, cfg->E, s) || upload_q(&m->ex.up, &w->up, cfg->E, s) ||
-             upload_q(&m->ex.down, &w->down, cfg->E, s) || upload_q(&m->ex.sh_gate, &w->sh_gate, 1, s) ||
+    const int El = m->E_loc, e0 = m->e0;
+    int rc = upload_q(&m->ex.gate, &w->gate, El, s, e0) || upload_q(&m->ex.up, &w->up, El, s, e0) ||
+             upload_q(&m->ex.down, &w->down, El, s, e0) || upload_q(&m->ex.sh_gate, &w->sh_gate, 1, s) ||
              upload_q(&m->ex.sh_up, &w->sh_up, 1, s) || upload_q(&m->ex.sh_down, &w->sh_down, 1, s);
     if (!rc && cfg->router_mode == QE_ROUTER_QMAT)
         rc = upload_q(&m->router_q, &w->router_q, 1, s) || upload_q(&m->sh_router_q, &w->sh_router_q, 1, s);
@@ -410,11 +427,12 @@ QeMoe *qe_moe_create_synthetic(const QeMoeConfig *cfg, uint64_t seed, uint32_t b
     if (!m) return nullptr;
     cudaStream_t s = g_dev[m->device].stream;
     const int E = cfg->E, H = cfg->hidden, I = cfg->inter, Is = cfg->sh_inter, b = cfg->bits, gs = cfg->group_size;
-    auto gen = [&](const QeQDev &q, uint32_t stream, int n) {
-        return qe_launch_synth_qmat(seed, block, stream, n, q.rows, q.cols, q.bits, gs, q.scale_t, (uint32_t *)q.w,
-                                    (uint16_t *)q.scales, (uint16_t *)q.biases, s);
+    auto gen = [&](const QeQDev &q, uint32_t stream, int n, int first = 0) {
+        return qe_launch_synth_qmat(seed, block, stream, first, n, q.rows, q.cols, q.bits, gs, q.scale_t,
+                                    (uint32_t *)q.w, (uint16_t *)q.scales, (uint16_t *)q.biases, s);
     };
-    int rc = gen(m->ex.gate, SYN_GATE, E) || gen(m->ex.up, SYN_UP, E) || gen(m->ex.down, SYN_DOWN, E) ||
+    const int El = m->E_loc, e0 = m->e0;
+    int rc = gen(m->ex.gate, SYN_GATE, El, e0) || gen(m->ex.up, SYN_UP, El, e0) || gen(m->ex.down, SYN_DOWN, El, e0) ||
              gen(m->ex.sh_gate, SYN_SH_GATE, 1) || gen(m->ex.sh_up, SYN_SH_UP, 1) || gen(m->ex.sh_down, SYN_SH_DOWN, 1);
     (void)I; (void)Is; (void)b;
     if (!rc && cfg->router_mode == QE_ROUTER_QMAT)
@@ -486,7 +504,7 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
         const int R = qe_tc_bm(), NB = qe_tc_bn();
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
                   tiles_dn = (c.hidden + R - 1) / R;
-        if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s)) return -1;
+        if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s)) return -1;
         prof_mark(dev, s);
         if (qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, T, sc.act, sc.actsum, sc.h3s, sc.h3sum, I, sms, s))
             return -1;
@@ -501,7 +519,7 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     const int R = qe_expert_rows_per_cta();
     const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R, tiles_dn = (c.hidden + R - 1) / R;
     const int chunk = T < 8 ? T : 8;
-    if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, tiles_gu, tiles_sh, tiles_dn, chunk, &sc.b, s)) return -1;
+    if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, tiles_gu, tiles_sh, tiles_dn, chunk, &sc.b, s)) return -1;
     prof_mark(dev, s);
     /* grid: enough CTAs for every item in the common case, grid-stride beyond */
     const long long slots = std::min<long long>((long long)c.E, (long long)T * c.top_k) + 1;
@@ -516,6 +534,150 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     if (qe_launch_combine(sc.ybuf, sc.score, sc.logits, c.E + 1, T, c.E, c.top_k, c.hidden, out, s)) return -1;
     prof_mark(dev, s);
     g_launches += 4;
+    return 0;
+}
+
+/* ------------------------------------------------------------------ expert parallelism */
+
+/* meta[T][2k]: the routing result per token, global expert ids then the scores' bits */
+__global__ void ep_meta_kernel(const int32_t *__restrict__ idx, const float *__restrict__ score, int T, int k,
+                               int32_t *__restrict__ meta) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= T * k) return;
+    const int t = i / k, j = i % k;
+    meta[(size_t)t * 2 * k + j] = idx[i];
+    meta[(size_t)t * 2 * k + k + j] = __float_as_int(score[i]);
+}
+
+/* meta (global ids) -> local slot ids of the experts [e0, e0 + El) (-1 elsewhere) and the scores */
+__global__ void ep_local_kernel(const int32_t *__restrict__ meta, int n, int k, int e0, int El,
+                                int32_t *__restrict__ idx, float *__restrict__ score) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * k) return;
+    const int t = i / k, j = i % k;
+    const int e = meta[(size_t)t * 2 * k + j];
+    idx[i] = (e >= e0 && e < e0 + El) ? e - e0 : -1;
+    score[i] = __int_as_float(meta[(size_t)t * 2 * k + k + j]);
+}
+
+/* One block per destination rank d: home[d][t] = the row of token t in block d (the tokens with at least one
+ * expert on d, in token order) or -1, counts[d] = rows in block d. */
+__global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *__restrict__ meta, int T, int k, int El,
+                                                       int32_t *__restrict__ home, int32_t *__restrict__ counts) {
+    const int d = blockIdx.x;
+    __shared__ int wsum[32];
+    __shared__ int base_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) base_s = 0;
+    __syncthreads();
+    for (int t0 = 0; t0 < T; t0 += 1024) {
+        const int t = t0 + tid;
+        int f = 0;
+        if (t < T)
+            for (int j = 0; j < k; j++) {
+                const int e = meta[(size_t)t * 2 * k + j];
+                f |= (e >= 0 && e / El == d) ? 1 : 0;
+            }
+        int incl = f;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(QE_FULL, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) wsum[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            const int w = wsum[lane];
+            int wi = w;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(QE_FULL, wi, o);
+                if (lane >= o) wi += v;
+            }
+            wsum[lane] = wi - w;
+        }
+        __syncthreads();
+        const int base = base_s;
+        if (t < T) home[(size_t)d * T + t] = f ? base + wsum[warp] + incl - f : -1;
+        __syncthreads();
+        if (tid == 1023) base_s = base + wsum[31] + incl;
+        __syncthreads();
+    }
+    if (tid == 0) counts[d] = base_s;
+}
+
+/* Warp (d, t): token t's row and meta to its row of block d; row t of block d, when at or past counts[d],
+ * becomes padding (expert ids -1, scores 0). H % 4 == 0, 16-byte aligned rows. */
+__global__ void ep_scatter_kernel(const float *__restrict__ x, const int32_t *__restrict__ meta, int T, int H, int k,
+                                  int G, const int32_t *__restrict__ home, const int32_t *__restrict__ counts,
+                                  float *__restrict__ send_x, int32_t *__restrict__ send_meta) {
+    const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= (long long)G * T) return;
+    const int d = (int)(w / T), t = (int)(w % T);
+    const int pos = home[(size_t)d * T + t];
+    if (pos >= 0) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * H);
+        float4 *dst = reinterpret_cast<float4 *>(send_x + ((size_t)d * T + pos) * H);
+        for (int c = lane; c < H / 4; c += 32) dst[c] = src[c];
+        for (int c = lane; c < 2 * k; c += 32) send_meta[((size_t)d * T + pos) * 2 * k + c] = meta[(size_t)t * 2 * k + c];
+    }
+    if (t >= counts[d])
+        for (int c = lane; c < 2 * k; c += 32) send_meta[((size_t)d * T + t) * 2 * k + c] = c < k ? -1 : 0;
+}
+
+/* out[t] = (sum over ranks d ascending of part[d][home[d][t]], skipping -1) + shared[t]; home NULL: part[d][t] */
+__global__ void ep_combine_kernel(const float *__restrict__ part, const int32_t *__restrict__ home,
+                                  const float *__restrict__ shared, int T, int G, int H, float *__restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)T * H) return;
+    const int t = (int)(i / H), c = (int)(i % H);
+    float o = 0.0f;
+    for (int d = 0; d < G; d++) {
+        const int pos = home ? home[(size_t)d * T + t] : t;
+        if (pos >= 0) o = __fadd_rn(o, part[((size_t)d * T + pos) * H + c]);
+    }
+    out[i] = __fadd_rn(o, shared[i]);
+}
+
+/* The expert stages for n rows whose local slot ids and scores are in sc.idx / sc.score (and, for the shared
+ * expert, whose gate logits are in sc.logits): bucket, gate/up + SwiGLU, down, then the selective combine. */
+int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sms, bool routed, bool shared,
+                cudaStream_t s) {
+    const QeMoeConfig &c = m->cfg;
+    const int El = m->E_loc, k = c.top_k;
+    const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
+    const int sh_tokens = shared ? n : 0;
+    const bool use_tc = m->tc && (m->path == 2 || (m->path == 0 && n >= kTcMinTokens));
+    if (use_tc) {
+        const int R = qe_tc_bm(), NB = qe_tc_bn();
+        const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
+                  tiles_dn = (c.hidden + R - 1) / R;
+        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s) ||
+            qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, n, sc.act, sc.actsum, sc.h3s, sc.h3sum, I, sms, s) ||
+            qe_launch_tc_down(&m->ex, m->maps_dn, sc.h3s, sc.h3sum, I, &sc.b, n, sc.ybuf, sms, s))
+            return -1;
+        g_launches += 4;
+    } else {
+        const int R = qe_expert_rows_per_cta();
+        const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
+                  tiles_dn = (c.hidden + R - 1) / R;
+        const int chunk = n < 8 ? n : 8;
+        const long long slots = std::min<long long>((long long)El, (long long)n * k) + 1;
+        const long long chunks = ((long long)n * (k + 1) + chunk - 1) / chunk + slots;
+        const int tmax = std::max(tiles_gu, tiles_sh);
+        const int grid_gu = (int)std::min<long long>(chunks * tmax, 16LL * sms);
+        const int grid_dn = (int)std::min<long long>(chunks * tiles_dn, 16LL * sms);
+        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, chunk, &sc.b, s) ||
+            qe_launch_gateup(&m->ex, x, &sc.b, n, sc.h3, I, grid_gu, s) ||
+            qe_launch_down(&m->ex, sc.h3, I, &sc.b, n, sc.ybuf, grid_dn, s))
+            return -1;
+        g_launches += 3;
+    }
+    if (qe_launch_combine_sel(sc.ybuf, sc.idx, sc.score, sc.logits, c.E + 1, n, c.E, k, c.hidden, routed ? 1 : 0,
+                              shared ? 1 : 0, out, s))
+        return -1;
+    g_launches += 1;
     return 0;
 }
 
@@ -543,6 +705,8 @@ extern "C" {
 
 int qe_moe_forward_device(QeMoe *m, int T, const float *x, float *out, void *stream) {
     if (!m || !x || !out || T < 1) QE_FAIL("forward: bad arguments");
+    if (m->cfg.ep_size > 1) QE_FAIL("forward: this handle holds experts [%d, %d) only: use the qe_moe_ep_* calls",
+                                    m->e0, m->e0 + m->E_loc);
     DevCtx *d;
     if (dev_ctx(m->device, &d)) return -1;
     cudaStream_t s = (cudaStream_t)stream;
@@ -560,6 +724,8 @@ int qe_moe_forward_device(QeMoe *m, int T, const float *x, float *out, void *str
 
 int qe_moe_forward(QeMoe *m, int T, const float *x, float *out) {
     if (!m || !x || !out || T < 1) QE_FAIL("forward: bad arguments");
+    if (m->cfg.ep_size > 1) QE_FAIL("forward: this handle holds experts [%d, %d) only: use the qe_moe_ep_* calls",
+                                    m->e0, m->e0 + m->E_loc);
     DevCtx *d;
     if (dev_ctx(m->device, &d)) return -1;
     cudaStream_t s = d->stream;
@@ -614,6 +780,83 @@ int qe_moe_route(QeMoe *m, int T, const float *x, int32_t *idx, float *score) {
         QE_CHECK(cudaMemcpyAsync(score + (size_t)t0 * k, sc.score, 4 * n * k, cudaMemcpyDeviceToHost, s));
         QE_CHECK(cudaStreamSynchronize(s));
     }
+    return 0;
+}
+
+int qe_moe_ep_size(const QeMoe *m) { return m ? m->cfg.ep_size : -1; }
+
+int qe_moe_ep_route_device(QeMoe *m, int T, const float *x, int32_t *meta, float *shared, void *stream) {
+    if (!m || !x || !meta || !shared || T < 1) QE_FAIL("ep_route: bad arguments");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int P = std::min(T, m->cfg.max_tokens), k = m->cfg.top_k;
+    const size_t H = m->cfg.hidden;
+    if (ensure_ws(d, scratch_layout(m->cfg, P, nullptr, nullptr))) return -1;
+    Scratch sc;
+    scratch_layout(m->cfg, P, (char *)d->ws, &sc);
+    for (int t0 = 0; t0 < T; t0 += P) {
+        const int n = std::min(P, T - t0);
+        if (run_route(m, x + (size_t)t0 * H, n, sc, s)) return -1;
+        ep_meta_kernel<<<(n * k + 255) / 256, 256, 0, s>>>(sc.idx, sc.score, n, k, meta + (size_t)t0 * 2 * k);
+        QE_CHECK(cudaGetLastError());
+        QE_CHECK(cudaMemsetAsync(sc.idx, 0xff, sizeof(int32_t) * (size_t)n * k, s));   /* shared expert only */
+        if (run_experts(m, x + (size_t)t0 * H, shared + (size_t)t0 * H, n, sc, d->sms, false, true, s)) return -1;
+        g_launches += 3;
+    }
+    return 0;
+}
+
+int qe_moe_ep_pack_device(QeMoe *m, int T, const float *x, const int32_t *meta, float *send_x, int32_t *send_meta,
+                          int32_t *home, int32_t *counts, void *stream) {
+    if (!m || !x || !meta || !send_x || !send_meta || !home || !counts || T < 1) QE_FAIL("ep_pack: bad arguments");
+    const int H = m->cfg.hidden, k = m->cfg.top_k, G = m->cfg.ep_size;
+    if (H % 4 || ((uintptr_t)x | (uintptr_t)send_x) % 16) QE_FAIL("ep_pack: x and send_x must be 16-byte aligned");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = (cudaStream_t)stream;
+    ep_plan_kernel<<<G, 1024, 0, s>>>(meta, T, k, m->E_loc, home, counts);
+    QE_CHECK(cudaGetLastError());
+    const long long threads = (long long)G * T * 32;
+    ep_scatter_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, meta, T, H, k, G, home, counts, send_x,
+                                                                       send_meta);
+    QE_CHECK(cudaGetLastError());
+    g_launches += 2;
+    return 0;
+}
+
+int qe_moe_ep_experts_device(QeMoe *m, int n, const float *x, const int32_t *meta, float *partial, void *stream) {
+    if (!m || !x || !meta || !partial || n < 1) QE_FAIL("ep_experts: bad arguments");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int P = std::min(n, m->cfg.max_tokens), k = m->cfg.top_k;
+    const size_t H = m->cfg.hidden;
+    if (ensure_ws(d, scratch_layout(m->cfg, P, nullptr, nullptr))) return -1;
+    Scratch sc;
+    scratch_layout(m->cfg, P, (char *)d->ws, &sc);
+    for (int r0 = 0; r0 < n; r0 += P) {
+        const int cnt = std::min(P, n - r0);
+        ep_local_kernel<<<(cnt * k + 255) / 256, 256, 0, s>>>(meta + (size_t)r0 * 2 * k, cnt, k, m->e0, m->E_loc,
+                                                             sc.idx, sc.score);
+        QE_CHECK(cudaGetLastError());
+        if (run_experts(m, x + (size_t)r0 * H, partial + (size_t)r0 * H, cnt, sc, d->sms, true, false, s)) return -1;
+        g_launches += 1;
+    }
+    return 0;
+}
+
+int qe_moe_ep_combine_device(QeMoe *m, int T, const float *part, const int32_t *home, const float *shared, float *out,
+                             void *stream) {
+    if (!m || !part || !shared || !out || T < 1) QE_FAIL("ep_combine: bad arguments");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    const long long n = (long long)T * m->cfg.hidden;
+    ep_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(part, home, shared, T,
+                                                                                     m->cfg.ep_size,
+                                                                                     m->cfg.hidden, out);
+    QE_CHECK(cudaGetLastError());
+    g_launches += 1;
     return 0;
 }
 

@@ -31,9 +31,10 @@ class MoeBlock:
     def __init__(self, hidden: int, E: int, top_k: int, inter: int, sh_inter: int, bits: int, group_size: int = 64,
                  *, router_mode: int = QE_ROUTER_F32, router_bits: int = 8, max_tokens: int = 4096, device: int = 0,
                  layer: int = 0, weights: Mapping | None = None, seed: int | None = None, block: int = 0,
-                 router_bias: np.ndarray | None = None):
+                 router_bias: np.ndarray | None = None, ep_rank: int = 0, ep_size: int = 1):
         self.cfg = QeMoeConfig(hidden, E, top_k, inter, sh_inter, bits, group_size, router_mode, router_bits,
-                               max_tokens, device, layer)
+                               max_tokens, device, layer, ep_rank, ep_size)
+        self.ep_rank, self.ep_size = ep_rank, ep_size
         self.hidden, self.top_k, self.E = hidden, top_k, E
         L = lib()
         self._keep = []

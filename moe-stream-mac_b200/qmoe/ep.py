@@ -1,0 +1,114 @@
+"""Expert parallelism: one routed MoE block sharded by expert over the ranks of a torch.distributed group.
+
+The reference runs the block in one process (engine/src/moe_layer.c:66-89). Here expert e lives on rank
+e // (E / world); the router and the shared expert are replicated. Two step shapes:
+
+* token-sharded (prefill batches): every rank routes its own tokens, packs for each destination rank the rows
+  of its tokens that have at least one expert there (token order, padded to T rows per destination so the
+  exchange is one all_to_all with equal blocks and needs no host round trip for the counts), exchanges rows
+  and slot lists, computes the partial sums of the slots it owns, sends them back, and sums the partials in
+  rank order plus the gated shared expert;
+* replicated (decode): every rank holds the same tokens, computes the partial sums of its own experts, and
+  the partials are all-gathered and summed in rank order (deterministic, unlike a reduction whose order
+  depends on the collective's algorithm).
+
+The arithmetic runs in an engine: `DeviceEngine` calls libqengine_b200's qe_moe_ep_* entry points on the
+rank's GPU (the product path). Tests substitute a CPU engine with the same contract to check the exchange
+logic under the gloo backend.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+import torch.distributed as dist
+
+from .block import EngineError, MoeBlock
+from .lib import lib
+
+
+class DeviceEngine:
+    """The qe_moe_ep_* calls of include/qe_moe.h on one handle (device tensors, torch's current stream)."""
+
+    def __init__(self, block: MoeBlock):
+        self.block = block
+        self.hidden, self.top_k = block.hidden, block.top_k
+
+    def _s(self) -> C.c_void_p:
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    @staticmethod
+    def _p(t: torch.Tensor | None) -> C.c_void_p:
+        return C.c_void_p(t.data_ptr() if t is not None else None)
+
+    def route(self, x, meta, shared):
+        if lib().qe_moe_ep_route_device(self.block.handle, x.shape[0], self._p(x), self._p(meta), self._p(shared),
+                                        self._s()):
+            raise EngineError("qe_moe_ep_route_device failed")
+
+    def pack(self, x, meta, send_x, send_meta, home, counts):
+        if lib().qe_moe_ep_pack_device(self.block.handle, x.shape[0], self._p(x), self._p(meta), self._p(send_x),
+                                       self._p(send_meta), self._p(home), self._p(counts), self._s()):
+            raise EngineError("qe_moe_ep_pack_device failed")
+
+    def experts(self, x, meta, partial):
+        if lib().qe_moe_ep_experts_device(self.block.handle, x.shape[0], self._p(x), self._p(meta),
+                                          self._p(partial), self._s()):
+            raise EngineError("qe_moe_ep_experts_device failed")
+
+    def combine(self, part, home, shared, out):
+        if lib().qe_moe_ep_combine_device(self.block.handle, out.shape[0], self._p(part), self._p(home),
+                                          self._p(shared), self._p(out), self._s()):
+            raise EngineError("qe_moe_ep_combine_device failed")
+
+
+class ExpertParallelMoe:
+    """One routed MoE block, experts sharded over `group` (default: the world), one rank per GPU."""
+
+    def __init__(self, engine, rank: int, world: int, group=None, device: torch.device | str = "cuda"):
+        self.engine, self.rank, self.world, self.group = engine, rank, world, group
+        self.device = torch.device(device)
+        self.hidden, self.top_k = engine.hidden, engine.top_k
+        self.last_counts: torch.Tensor | None = None   # rows sent to each rank by the last sharded step
+
+    @classmethod
+    def on_gpu(cls, cfg, rank: int, world: int, device: int, *, seed: int, block: int = 0, router_bias=None,
+               max_tokens: int = 4096, group=None) -> "ExpertParallelMoe":
+        """A synthetic block (qmoe.synth.MoeConfig shape) holding experts [rank*E/world, (rank+1)*E/world)."""
+        blk = MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, max_tokens=max_tokens,
+                       device=device, seed=seed, block=block, router_bias=router_bias, ep_rank=rank, ep_size=world)
+        return cls(DeviceEngine(blk), rank, world, group, torch.device("cuda", device))
+
+    def _empty(self, *shape, dtype=torch.float32):
+        return torch.empty(*shape, dtype=dtype, device=self.device)
+
+    def forward(self, x: torch.Tensor, mode: str = "sharded") -> torch.Tensor:
+        """out[T][hidden] for this rank's x[T][hidden] (sharded), or for the tokens every rank holds
+        (replicated). Every rank must call it with the same T and mode."""
+        if mode not in ("sharded", "replicated"):
+            raise ValueError(f"mode {mode!r}")
+        T, H, k, G = x.shape[0], self.hidden, self.top_k, self.world
+        meta = self._empty(T, 2 * k, dtype=torch.int32)
+        shared = self._empty(T, H)
+        out = self._empty(T, H)
+        self.engine.route(x, meta, shared)
+        if mode == "replicated":
+            partial = self._empty(T, H)
+            self.engine.experts(x, meta, partial)
+            parts = self._empty(G, T, H)
+            dist.all_gather_into_tensor(parts.view(G * T, H), partial, group=self.group)
+            self.engine.combine(parts, None, shared, out)
+            return out
+        send_x, send_meta = self._empty(G, T, H), self._empty(G, T, 2 * k, dtype=torch.int32)
+        home, counts = self._empty(G, T, dtype=torch.int32), self._empty(G, dtype=torch.int32)
+        self.engine.pack(x, meta, send_x, send_meta, home, counts)
+        recv_x, recv_meta = torch.empty_like(send_x), torch.empty_like(send_meta)
+        dist.all_to_all_single(recv_x, send_x, group=self.group)
+        dist.all_to_all_single(recv_meta, send_meta, group=self.group)
+        partial = self._empty(G, T, H)
+        self.engine.experts(recv_x.view(G * T, H), recv_meta.view(G * T, 2 * k), partial.view(G * T, H))
+        back = torch.empty_like(partial)
+        dist.all_to_all_single(back, partial, group=self.group)
+        self.engine.combine(back, home, shared, out)
+        self.last_counts = counts
+        return out

@@ -17,7 +17,8 @@ QE_ROUTER_QMAT = 1
 class QeMoeConfig(C.Structure):
     _fields_ = [("hidden", C.c_int), ("E", C.c_int), ("top_k", C.c_int), ("inter", C.c_int), ("sh_inter", C.c_int),
                 ("bits", C.c_int), ("group_size", C.c_int), ("router_mode", C.c_int), ("router_bits", C.c_int),
-                ("max_tokens", C.c_int), ("device", C.c_int), ("layer", C.c_int)]
+                ("max_tokens", C.c_int), ("device", C.c_int), ("layer", C.c_int), ("ep_rank", C.c_int),
+                ("ep_size", C.c_int)]
 
 
 class QeQTensor(C.Structure):
@@ -70,6 +71,11 @@ def lib() -> C.CDLL:
         L.qe_kernel_launches.restype = C.c_ulonglong
         L.qe_device_error.restype = C.c_int
         L.qe_route_f32_noalloc.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp]
+        L.qe_moe_ep_route_device.argtypes = [vp, C.c_int, vp, vp, vp, vp]
+        L.qe_moe_ep_pack_device.argtypes = [vp, C.c_int, vp, vp, vp, vp, vp, vp, vp]
+        L.qe_moe_ep_experts_device.argtypes = [vp, C.c_int, vp, vp, vp, vp]
+        L.qe_moe_ep_combine_device.argtypes = [vp, C.c_int, vp, vp, vp, vp, vp]
+        L.qe_moe_ep_size.argtypes = [vp]
         _lib = L
     return _lib
 

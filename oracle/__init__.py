@@ -70,6 +70,8 @@ def lib() -> C.CDLL:
         L.or_route_from_logits.argtypes = [fp, C.c_int, C.c_int, fp, ip, fp]
         L.or_moe_step.argtypes = [C.POINTER(OrBlock), fp, fp, ip, fp]
         L.or_moe_forward.argtypes = [C.POINTER(OrBlock), C.c_int, fp, fp, ip, fp]
+        L.or_expert_mlp.argtypes = [C.POINTER(OrBlock), C.c_int, fp, fp]
+        L.or_shared_gate_logit.argtypes = [C.POINTER(OrBlock), fp, fp]
         L.or_synth_block.restype = C.POINTER(OrBlock)
         L.or_synth_block.argtypes = [C.POINTER(OrSynthCfg), C.c_uint64, C.c_uint32, fp]
         L.or_free_block.argtypes = [C.POINTER(OrBlock)]
@@ -183,6 +185,19 @@ class SynthBlock:
         if ref().ref_b_forward(self.ptr, T, fptr(np.ascontiguousarray(x)), fptr(out), iptr(idx), fptr(score)):
             raise RuntimeError("ref_b_forward failed")
         return out, idx, score
+
+    def expert(self, e: int, x: np.ndarray) -> np.ndarray:
+        """One expert's MLP on one token (e = -1: the shared expert), moe_layer.c:20-26."""
+        y = np.empty(self.cfg.hidden, np.float32)
+        if lib().or_expert_mlp(self.ptr, e, fptr(np.ascontiguousarray(x, np.float32)), fptr(y)):
+            raise RuntimeError("or_expert_mlp failed")
+        return y
+
+    def shared_gate_logit(self, x: np.ndarray) -> np.float32:
+        g = np.empty(1, np.float32)
+        if lib().or_shared_gate_logit(self.ptr, fptr(np.ascontiguousarray(x, np.float32)), fptr(g)):
+            raise RuntimeError("or_shared_gate_logit failed")
+        return g[0]
 
     def router_logits(self, x: np.ndarray) -> np.ndarray:
         T = x.shape[0]

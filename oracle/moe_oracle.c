@@ -220,6 +220,32 @@ done:
     return rc;
 }
 
+/* One expert's SwiGLU MLP (moe_layer.c:20-26): e in [0, E) a routed expert, e = -1 the shared expert. */
+int or_expert_mlp(const OrBlock *b, int e, const float *x, float *y) {
+    if (e < -1 || e >= b->E) return -1;
+    const int m = b->inter > b->sh_inter ? b->inter : b->sh_inter;
+    float *buf = malloc(sizeof(float) * (size_t)(3 * m));
+    if (!buf) return -1;
+    int rc;
+    if (e < 0) {
+        rc = mlp(&b->sh_gate, &b->sh_up, &b->sh_down, x, y, buf, buf + m, buf + 2 * m);
+    } else {
+        const OrQMat g = or_qmat_expert(&b->gate, e), u = or_qmat_expert(&b->up, e), d = or_qmat_expert(&b->down, e);
+        rc = mlp(&g, &u, &d, x, y, buf, buf + m, buf + 2 * m);
+    }
+    free(buf);
+    return rc;
+}
+
+/* The shared-expert gate logit (moe_layer.c:85-87): w_sg . x in fp32 mode, else the shared_expert_gate QMat. */
+int or_shared_gate_logit(const OrBlock *b, const float *x, float *g) {
+    if (b->sh_gate_f32) {
+        g[0] = or_dot_f32(b->sh_gate_f32, x, b->hidden);
+        return 0;
+    }
+    return or_qmat_matvec(&b->sh_router_q, x, g);
+}
+
 /* T independent tokens (the reference has no batched prefill, docs/C_ENGINE.md:81: prefill is T calls
  * of moe_layer_step). Tokens run in parallel here; each token's arithmetic is unchanged. */
 int or_moe_forward(const OrBlock *b, int T, const float *x, float *out, int *idx, float *score) {

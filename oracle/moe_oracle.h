@@ -55,6 +55,8 @@ int or_router_logits(const OrBlock *b, const float *x, float *logits);
 int or_route_from_logits(const float *logits, int E, int k, float *probs, int *idx, float *score);
 int or_moe_step(const OrBlock *b, const float *x, float *out, int *idx, float *score);
 int or_moe_forward(const OrBlock *b, int T, const float *x, float *out, int *idx, float *score);
+int or_expert_mlp(const OrBlock *b, int e, const float *x, float *y);
+int or_shared_gate_logit(const OrBlock *b, const float *x, float *g);
 
 /* Synthetic block generation (moe-stream-mac_b200/csrc/synth.h), for tests and the CPU baseline. */
 typedef struct {

@@ -1,0 +1,167 @@
+"""Expert parallelism on the GPU: the qe_moe_ep_* entry points of include/qe_moe.h.
+
+On one GPU the ranks are emulated: G handles, each holding E/G experts, run the token-sharded step with the
+all_to_all done by tensor slicing (every launch completes before the next; nothing waits on another rank).
+Results are compared with the single-handle forward (routing bit-identical; outputs within the fp32 regrouping
+of the sum by rank) and with the oracle. With two or more GPUs, the same step runs over NCCL in one process per
+GPU (qmoe.ep.ExpertParallelMoe)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import qmoe
+
+pytestmark = pytest.mark.gpu
+
+CFG = qmoe.MoeConfig("ep_small", hidden=512, inter=256, sh_inter=256, bits=4, tokens=64, E=32, top_k=4)
+
+
+def _blocks(cfg, G, seed=5):
+    return [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, seed=seed,
+                          ep_rank=r, ep_size=G) for r in range(G)]
+
+
+def _emulated_sharded_step(blocks, xs):
+    """The token-sharded step of qmoe.ep with G emulated ranks on one GPU; xs[r] = rank r's tokens [T][H]."""
+    from qmoe.ep import DeviceEngine
+    G, T, H = len(blocks), xs[0].shape[0], xs[0].shape[1]
+    eng = [DeviceEngine(b) for b in blocks]
+    k = blocks[0].top_k
+    dev = xs[0].device
+    meta = [torch.empty(T, 2 * k, dtype=torch.int32, device=dev) for _ in range(G)]
+    shared = [torch.empty(T, H, device=dev) for _ in range(G)]
+    send_x = [torch.empty(G, T, H, device=dev) for _ in range(G)]
+    send_m = [torch.empty(G, T, 2 * k, dtype=torch.int32, device=dev) for _ in range(G)]
+    home = [torch.empty(G, T, dtype=torch.int32, device=dev) for _ in range(G)]
+    counts = [torch.empty(G, dtype=torch.int32, device=dev) for _ in range(G)]
+    for r in range(G):
+        eng[r].route(xs[r], meta[r], shared[r])
+        eng[r].pack(xs[r], meta[r], send_x[r], send_m[r], home[r], counts[r])
+    # all_to_all: rank d receives block d of every source s, stacked by s
+    recv_x = [torch.stack([send_x[s][d] for s in range(G)]) for d in range(G)]
+    recv_m = [torch.stack([send_m[s][d] for s in range(G)]) for d in range(G)]
+    partial = [torch.empty(G, T, H, device=dev) for _ in range(G)]
+    for d in range(G):
+        eng[d].experts(recv_x[d].view(G * T, H), recv_m[d].view(G * T, 2 * k), partial[d].view(G * T, H))
+    back = [torch.stack([partial[d][s] for d in range(G)]) for s in range(G)]
+    outs = []
+    for r in range(G):
+        out = torch.empty(T, H, device=dev)
+        eng[r].combine(back[r], home[r], shared[r], out)
+        outs.append(out)
+    torch.cuda.synchronize()
+    return outs, [m.cpu().numpy() for m in meta], [c.cpu().numpy() for c in counts]
+
+
+def _rel(a, b):
+    return np.linalg.norm(a - b, axis=1) / np.maximum(np.linalg.norm(b, axis=1), 1e-30)
+
+
+@pytest.mark.parametrize("G,T", [(1, 64), (1, 8), (2, 64), (4, 32), (8, 16), (8, 3)])
+def test_ep_emulated_vs_single(G, T):
+    ref = qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5)
+    blocks = _blocks(CFG, G)
+    gen = torch.Generator().manual_seed(100 + G * 7 + T)
+    xs = [torch.randn(T, CFG.hidden, generator=gen).cuda() for _ in range(G)]
+    outs, metas, counts = _emulated_sharded_step(blocks, xs)
+    k = CFG.top_k
+    for r in range(G):
+        want = torch.empty_like(xs[r])
+        ref.forward_device(T, xs[r].data_ptr(), want.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        idx, score = ref.route(xs[r].cpu().numpy())
+        assert np.array_equal(metas[r][:, :k], idx)
+        assert np.array_equal(metas[r][:, k:].view(np.float32).view(np.uint32), score.view(np.uint32))
+        got, w = outs[r].cpu().numpy(), want.cpu().numpy()
+        # each rank's destinations: tokens with an expert on d
+        dests = (idx // (CFG.E // G))
+        for d in range(G):
+            assert counts[r][d] == int(np.any(dests == d, axis=1).sum())
+        if G == 1:
+            # one rank: same expert path (the experts call sees the same T rows), bit-identical
+            assert np.array_equal(got.view(np.uint32), w.view(np.uint32)), "ep_size 1 differs from forward"
+        else:
+            # regrouped fp32 sum, and the experts call may take the other expert path (G*T rows)
+            assert _rel(got, w).max() <= 5e-6
+    for b in blocks + [ref]:
+        b.close()
+
+
+def test_ep_vs_oracle():
+    G, T = 4, 24
+    cfg = oracle.BlockCfg(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits)
+    ob = oracle.SynthBlock(cfg, seed=9)
+    blocks = _blocks(CFG, G, seed=9)
+    xs_np = [ob.x(T, seed=300 + r) for r in range(G)]
+    outs, _, _ = _emulated_sharded_step(blocks, [torch.from_numpy(x).cuda() for x in xs_np])
+    for r in range(G):
+        want, _, _ = ob.forward(xs_np[r])
+        got = outs[r].cpu().numpy()
+        assert _rel(got, want).max() <= 1e-5
+        assert np.abs(got - want).max() <= 1e-4
+    for b in blocks:
+        b.close()
+
+
+def test_ep_refusals():
+    b = qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, ep_rank=1, ep_size=2)
+    x = np.zeros((2, CFG.hidden), np.float32)
+    with pytest.raises(qmoe.EngineError):
+        b.forward(x)   # a handle with half the experts has no whole-block forward
+    b.close()
+    with pytest.raises(qmoe.EngineError):
+        qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, ep_rank=0, ep_size=3)
+    with pytest.raises(qmoe.EngineError):
+        qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, ep_rank=2, ep_size=2)
+
+
+def _nccl_worker(rank, world, port, mode, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from qmoe.ep import ExpertParallelMoe
+        ep = ExpertParallelMoe.on_gpu(CFG, rank, world, rank, seed=5)
+        ref = qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, device=rank)
+        T = 48
+        gen = torch.Generator().manual_seed(1000 + (rank if mode == "sharded" else 0))
+        x = torch.randn(T, CFG.hidden, generator=gen).cuda(rank)
+        out = ep.forward(x, mode=mode)
+        want = torch.empty_like(x)
+        ref.forward_device(T, x.data_ptr(), want.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        q.put((rank, float(_rel(out.cpu().numpy(), want.cpu().numpy()).max())))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["sharded", "replicated"])
+def test_ep_nccl_two_gpus(mode):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.exitcode is None:
+            p.kill()
+    assert codes == [0, 0], codes
+    for _ in procs:
+        rank, rel = q.get(timeout=10)
+        assert rel <= 5e-6, (rank, rel)

@@ -8,7 +8,10 @@ One step = one forward of one MoE block over the configuration's token batch (co
 weights (4 x 453 MB, far above the 126 MB L2) are used in rotation, so no step finds its weights in L2.
 `value` is device-timed (CUDA events on the launching stream, inputs resident in HBM); `e2e` is the same
 metric through the public host-buffer call qe_moe_forward (pinned host x in, host out back, every step).
-Under torchrun every rank runs its own replica (weak scaling); value = tokens of all ranks / max rank time.
+Under torchrun (N > 1) the block is expert-parallel (qmoe.ep): rank r holds experts [r*E/N, (r+1)*E/N) of
+every block plus the replicated router and shared expert, routes its own 512 tokens, and exchanges rows and
+partial sums with all_to_all over NCCL (weak scaling: per-rank tokens fixed); value = tokens of all ranks /
+max rank time.
 --impl reference times the reference's own C engine (oracle/_ref, built from its sources) on the host.
 """
 from __future__ import annotations
@@ -152,12 +155,14 @@ def run_reference_arm(args, cfg):
     print(json.dumps(line))
 
 
-def workload_config(cfg, world):
+def workload_config(cfg, world, blocks=4):
+    mb = blocks * (cfg.E // world * cfg.expert_bytes + cfg.shared_bytes + 4 * cfg.E * cfg.hidden) / 1e6
     return {"workload": f"{cfg.name}: {cfg.note}", "tokens_per_step": cfg.tokens, "hidden": cfg.hidden,
             "experts": cfg.E, "top_k": cfg.top_k, "inter": cfg.inter, "sh_inter": cfg.sh_inter, "bits": cfg.bits,
             "group_size": cfg.group_size, "router": "fp32", "parallelism": "1 GPU" if world == 1 else
-            f"{world} independent replicas", "l2": "4 blocks with distinct weights rotated per step "
-                                                   f"({4 * 453} MB of weights > 126 MB L2)"}
+            f"expert parallel over {world} GPUs ({cfg.E // world} experts each; router and shared expert "
+            f"replicated; {cfg.tokens} tokens per GPU; all_to_all over NCCL)",
+            "l2": f"{blocks} blocks with distinct weights rotated per step ({mb:.0f} MB of weights per GPU > 126 MB L2)"}
 
 
 def stage_bytes(cfg, uniq: int, T: int) -> dict:
@@ -170,6 +175,54 @@ def stage_bytes(cfg, uniq: int, T: int) -> dict:
     gu = uniq * 2 * q(cfg.inter, cfg.hidden) + 2 * q(cfg.sh_inter, cfg.hidden) + 4 * T * cfg.hidden + 4 * npair * I
     dn = uniq * q(cfg.hidden, cfg.inter) + q(cfg.hidden, cfg.sh_inter) + 4 * npair * I + 4 * npair * cfg.hidden
     return {"gateup": gu, "down": dn}
+
+
+def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, nprof=10):
+    """Per-phase times of the expert-parallel step (CUDA events between phases, a separate run after the
+    timed region) and the roofline of its expert stage: this rank's touched experts' weights once, plus the
+    rows it receives and the partial sums it returns."""
+    import torch
+    names = ("route", "pack", "dispatch", "experts", "return", "combine")
+    acc = dict.fromkeys(names, 0.0)
+    for i in range(nprof):
+        evs = []
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+
+        def mark(name):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(stream)
+            evs.append((name, ev))
+        models[i % len(models)].forward(x, mark=mark)
+        torch.cuda.synchronize()
+        prev = e_start
+        for name, ev in evs:
+            acc[name] += prev.elapsed_time(ev)
+            prev = ev
+    phase_ms = {k: v / nprof for k, v in acc.items()}
+    # experts of this rank touched by any rank's tokens
+    idx, _ = models[0].engine.block.route(x.cpu().numpy())
+    allidx = torch.empty(world * idx.size, dtype=torch.int32, device="cuda")
+    torch.distributed.all_gather_into_tensor(allidx, torch.from_numpy(idx.reshape(-1)).cuda())
+    El = cfg.E // world
+    ids = allidx.cpu().numpy().reshape(-1, cfg.top_k)
+    local = (ids >= rank * El) & (ids < (rank + 1) * El)
+    uniq = len(np.unique(ids[local]))
+    rows, pairs = int(local.any(axis=1).sum()), int(local.sum())   # rows received, (row, expert) pairs
+    H, I = cfg.hidden, cfg.inter
+    # weights of the touched experts once; x rows in, partial rows out; h3 written and read; y per pair
+    nbytes = uniq * cfg.expert_bytes + 8 * rows * H + 8 * pairs * I + 4 * pairs * H
+    achieved = nbytes / (phase_ms["experts"] / 1e3) / 1e9
+    G, T = world, cfg.tokens
+    xbytes = (G - 1) * T * (4 * H + 8 * cfg.top_k)   # rows + slot lists sent to the other ranks (padded blocks)
+    return {"bound": "hbm", "kernel": f"expert stage (qe_moe_ep_experts_device) on rank {rank}", "achieved": achieved,
+            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None, "peak_source": peak_source,
+            "algorithmic_bytes_per_launch": nbytes, "unique_local_experts": uniq,
+            "phase_ms": {k: round(v, 5) for k, v in phase_ms.items()},
+            "exchange": {"bytes_sent_per_rank_each_way": xbytes,
+                         "dispatch_GBs": xbytes / (phase_ms["dispatch"] / 1e3) / 1e9 if phase_ms["dispatch"] else None,
+                         "return_GBs": (G - 1) * T * 4 * H / (phase_ms["return"] / 1e3) / 1e9
+                         if phase_ms["return"] else None}}
 
 
 def main():
@@ -200,17 +253,26 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local))
     T = cfg.tokens
-    blocks = [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size,
-                            max_tokens=T, device=local, seed=1000 * rank + b + 1, block=b)
-              for b in range(args.blocks)]
+    ep = world > 1
     gen = torch.Generator(device="cuda").manual_seed(7 + rank)
     x = torch.randn(T, cfg.hidden, device="cuda", generator=gen, dtype=torch.float32)
     out = torch.empty_like(x)
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
+    if ep:
+        from qmoe.ep import ExpertParallelMoe
+        models = [ExpertParallelMoe.on_gpu(cfg, rank, world, local, seed=b + 1, block=b, max_tokens=world * T)
+                  for b in range(args.blocks)]
+        blocks = [m.engine.block for m in models]
 
-    def step(i):
-        blocks[i % len(blocks)].forward_device(T, x.data_ptr(), out.data_ptr(), sptr)
+        def step(i):
+            models[i % len(models)].forward(x)
+    else:
+        blocks = [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size,
+                                max_tokens=T, device=local, seed=b + 1, block=b) for b in range(args.blocks)]
+
+        def step(i):
+            blocks[i % len(blocks)].forward_device(T, x.data_ptr(), out.data_ptr(), sptr)
 
     def barrier():
         if world > 1:
@@ -248,12 +310,21 @@ def main():
     oh = torch.empty_like(xh).pin_memory()
     xn, on = xh.numpy(), oh.numpy()
     ke = max(10, min(args.steps, 200))
+
+    def e2e_step(i):
+        if ep:   # qmoe.ep.ExpertParallelMoe.forward with the copies in and out of pinned host memory
+            xd = xh.to("cuda", non_blocking=True)
+            oh.copy_(models[i % len(models)].forward(xd), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        else:    # qe_moe_forward: host buffers in and out
+            blocks[i % len(blocks)].forward(xn, on)
+
     for i in range(3):
-        blocks[i % len(blocks)].forward(xn, on)
+        e2e_step(i)
     barrier()
     t0 = time.perf_counter()
     for i in range(ke):
-        blocks[i % len(blocks)].forward(xn, on)
+        e2e_step(i)
     barrier()
     e2e_s = time.perf_counter() - t0
     te = torch.tensor([e2e_s], device="cuda")
@@ -261,25 +332,29 @@ def main():
         torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
     e2e_value = world * T * ke / float(te.item())
 
-    # roofline of the dominant kernel (per-stage CUDA events recorded inside the timed region)
-    idx, _ = blocks[0].route(x.cpu().numpy())
-    uniq = len(np.unique(idx))
-    sb = stage_bytes(cfg, uniq, T)
-    top = max(("gateup", "down"), key=lambda s: stage_ms[s])
-    per_launch_ms = stage_ms[top] / max(passes, 1)
-    achieved = sb[top] / (per_launch_ms / 1e3) / 1e9
     peak, peak_kind = hbm_peak()
-    total_stage = sum(stage_ms.values())
-    roofline = {"bound": "hbm", "kernel": f"expert_kernel<{cfg.bits},{cfg.group_size},{top}>", "achieved": achieved,
-                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else
-                "fallback 6.65 TB/s", "algorithmic_bytes_per_launch": sb[top], "unique_experts": uniq,
-                "stage_share": {k: round(v / total_stage, 4) for k, v in stage_ms.items()},
-                "stage_ms_per_pass": {k: round(v / max(passes, 1), 5) for k, v in stage_ms.items()}}
+    peak_source = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s")
+    if ep:
+        roofline = ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source)
+    else:
+        # roofline of the dominant kernel (per-stage CUDA events recorded inside the timed region)
+        idx, _ = blocks[0].route(x.cpu().numpy())
+        uniq = len(np.unique(idx))
+        sb = stage_bytes(cfg, uniq, T)
+        top = max(("gateup", "down"), key=lambda s: stage_ms[s])
+        per_launch_ms = stage_ms[top] / max(passes, 1)
+        achieved = sb[top] / (per_launch_ms / 1e3) / 1e9
+        total_stage = sum(stage_ms.values())
+        roofline = {"bound": "hbm", "kernel": f"expert_kernel<{cfg.bits},{cfg.group_size},{top}>",
+                    "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                    "peak_source": peak_source, "algorithmic_bytes_per_launch": sb[top], "unique_experts": uniq,
+                    "stage_share": {k: round(v / total_stage, 4) for k, v in stage_ms.items()},
+                    "stage_ms_per_pass": {k: round(v / max(passes, 1), 5) for k, v in stage_ms.items()}}
 
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(cfg, world),
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(cfg, world, args.blocks),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * cfg.hidden,
                     "d2h_bytes_per_step": 4 * T * cfg.hidden, "steps": ke, "timing": "host clock, max over ranks"},
             "roofline": roofline, "gpu_launches": launches, "clocks": clk}

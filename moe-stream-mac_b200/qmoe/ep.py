@@ -82,33 +82,44 @@ class ExpertParallelMoe:
     def _empty(self, *shape, dtype=torch.float32):
         return torch.empty(*shape, dtype=dtype, device=self.device)
 
-    def forward(self, x: torch.Tensor, mode: str = "sharded") -> torch.Tensor:
+    def forward(self, x: torch.Tensor, mode: str = "sharded", mark=None) -> torch.Tensor:
         """out[T][hidden] for this rank's x[T][hidden] (sharded), or for the tokens every rank holds
-        (replicated). Every rank must call it with the same T and mode."""
+        (replicated). Every rank must call it with the same T and mode. mark(name), if given, is called
+        after each phase (route, pack, dispatch, experts, return, combine), e.g. to record CUDA events."""
         if mode not in ("sharded", "replicated"):
             raise ValueError(f"mode {mode!r}")
+        mark = mark or (lambda name: None)
         T, H, k, G = x.shape[0], self.hidden, self.top_k, self.world
         meta = self._empty(T, 2 * k, dtype=torch.int32)
         shared = self._empty(T, H)
         out = self._empty(T, H)
         self.engine.route(x, meta, shared)
+        mark("route")
         if mode == "replicated":
             partial = self._empty(T, H)
             self.engine.experts(x, meta, partial)
+            mark("experts")
             parts = self._empty(G, T, H)
             dist.all_gather_into_tensor(parts.view(G * T, H), partial, group=self.group)
+            mark("return")
             self.engine.combine(parts, None, shared, out)
+            mark("combine")
             return out
         send_x, send_meta = self._empty(G, T, H), self._empty(G, T, 2 * k, dtype=torch.int32)
         home, counts = self._empty(G, T, dtype=torch.int32), self._empty(G, dtype=torch.int32)
         self.engine.pack(x, meta, send_x, send_meta, home, counts)
+        mark("pack")
         recv_x, recv_meta = torch.empty_like(send_x), torch.empty_like(send_meta)
         dist.all_to_all_single(recv_x, send_x, group=self.group)
         dist.all_to_all_single(recv_meta, send_meta, group=self.group)
+        mark("dispatch")
         partial = self._empty(G, T, H)
         self.engine.experts(recv_x.view(G * T, H), recv_meta.view(G * T, 2 * k), partial.view(G * T, H))
+        mark("experts")
         back = torch.empty_like(partial)
         dist.all_to_all_single(back, partial, group=self.group)
+        mark("return")
         self.engine.combine(back, home, shared, out)
+        mark("combine")
         self.last_counts = counts
         return out

@@ -165,6 +165,31 @@ def workload_config(cfg, world, blocks=4):
             "l2": f"{blocks} blocks with distinct weights rotated per step ({mb:.0f} MB of weights per GPU > 126 MB L2)"}
 
 
+def profiled_traffic(kernel: str, config: str):
+    """DRAM bytes per launch (read + write) of `kernel` on `config` from the committed ncu summaries
+    (lines `dram_bytes_per_launch[<kernel>,<config>]: N` under profiles/), or None."""
+    import re
+    key = f"dram_bytes_per_launch[{kernel},{config}]:"
+    for f in sorted((REPO / "profiles").glob("*.md")):
+        for line in f.read_text().splitlines():
+            line = line.strip()
+            if line.startswith(key):
+                m = re.match(r".*:\s*(\d+)", line)
+                if m:
+                    return int(m.group(1)), f.name
+    return None
+
+
+def expert_kernel_name(cfg, stage: str, T: int) -> str:
+    """The kernel the library runs for this stage (tensor-core path for batches of 64 tokens or more when
+    the shape allows it: group size 64, every matrix a whole number of 128-row tiles)."""
+    tc = (T >= 64 and cfg.group_size == 64 and all(d % 128 == 0 for d in (cfg.hidden, cfg.inter, cfg.sh_inter))
+          and os.environ.get("QE_EXPERT_PATH", "auto") != "mma")
+    if tc:
+        return f"tc_expert_kernel<{cfg.bits},{2 if stage == 'gateup' else 1}>"
+    return f"expert_kernel<{cfg.bits},{cfg.group_size},{stage}>"
+
+
 def stage_bytes(cfg, uniq: int, T: int) -> dict:
     """Algorithmic bytes per launch of each expert kernel: every active expert's weights once, plus the
     activations the kernel must read and write (fp32)."""
@@ -345,8 +370,13 @@ def main():
         per_launch_ms = stage_ms[top] / max(passes, 1)
         achieved = sb[top] / (per_launch_ms / 1e3) / 1e9
         total_stage = sum(stage_ms.values())
-        roofline = {"bound": "hbm", "kernel": f"expert_kernel<{cfg.bits},{cfg.group_size},{top}>",
-                    "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+        kname = expert_kernel_name(cfg, top, T)
+        tr = profiled_traffic(kname, cfg.name)
+        roofline = {"bound": "hbm", "kernel": kname + (" (gate/up + SwiGLU)" if top == "gateup" else " (down)"),
+                    "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                    "traffic": tr[0] if tr else None,
+                    "traffic_source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/{tr[1]}" if tr
+                    else "no ncu capture committed for this kernel and config",
                     "peak_source": peak_source, "algorithmic_bytes_per_launch": sb[top], "unique_experts": uniq,
                     "stage_share": {k: round(v / total_stage, 4) for k, v in stage_ms.items()},
                     "stage_ms_per_pass": {k: round(v / max(passes, 1), 5) for k, v in stage_ms.items()}}

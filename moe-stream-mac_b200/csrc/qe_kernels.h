@@ -18,7 +18,9 @@ struct QeQDev {
 /* Routing: fp32 router logits for E experts plus one extra column (index E) holding the shared-expert
  * gate logit, logits[T][E+1]. */
 int qe_launch_router_f32(const float *W /*[E+1][H]*/, const float *bias /*[E] or null*/, const float *x,
-                         int T, int H, int E, float *logits, cudaStream_t s);
+                         int T, int H, int E, float *logits,
+                         float *part /* [ceil(H/64)][T][E+1] scratch for the chunk-split prefill GEMM, or null */,
+                         cudaStream_t s);
 int qe_launch_router_qmat(const QeQDev *router /*[E][H]*/, const QeQDev *sh_router /*[1][H]*/, const float *x,
                           int T, int H, int E, float *logits, cudaStream_t s);
 int qe_launch_route_topk(const float *logits, int ld, int T, int E, int k, int32_t *idx, float *score,

@@ -112,6 +112,7 @@ size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 /* Carves a workspace into the per-forward buffers. */
 struct Scratch {
     float *x, *out, *logits, *score, *h3, *ybuf;
+    float *rpart;               /* fp32 router chunk values [hidden/64][T][E+1] (prefill GEMM) */
     int32_t *idx;
     QeBuckets b;
     __nv_bfloat16 *act, *h3s;   /* tensor-core path: split activations [3][npairs][K] */
@@ -131,6 +132,7 @@ size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
     t.x = (float *)take(sizeof(float) * (size_t)T * c.hidden);
     t.out = (float *)take(sizeof(float) * (size_t)T * c.hidden);
     t.logits = (float *)take(sizeof(float) * (size_t)T * (E + 1));
+    t.rpart = (float *)take(sizeof(float) * (size_t)((c.hidden + 63) / 64) * T * (E + 1));
     t.score = (float *)take(sizeof(float) * (size_t)T * k);
     t.idx = (int32_t *)take(sizeof(int32_t) * (size_t)T * k);
     t.h3 = (float *)take(sizeof(float) * npair * I);
@@ -476,7 +478,7 @@ namespace {
 int run_route(QeMoe *m, const float *x, int T, Scratch &sc, cudaStream_t s) {
     const QeMoeConfig &c = m->cfg;
     if (c.router_mode == QE_ROUTER_F32) {
-        if (qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, s)) return -1;
+        if (qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, sc.rpart, s)) return -1;
     } else {
         if (qe_launch_router_qmat(&m->router_q, &m->sh_router_q, x, T, c.hidden, c.E, sc.logits, s)) return -1;
     }
@@ -488,7 +490,7 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     const int dev = m->device;
     prof_mark(dev, s);
     if (c.router_mode == QE_ROUTER_F32) {
-        if (qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, s)) return -1;
+        if (qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, sc.rpart, s)) return -1;
         g_launches += 1;
     } else {
         if (qe_launch_router_qmat(&m->router_q, &m->sh_router_q, x, T, c.hidden, c.E, sc.logits, s)) return -1;

@@ -77,18 +77,23 @@ __global__ void __launch_bounds__(128) router_gemv_f32_kernel(const float *__res
 /* Prefill: 64 router rows x 32 tokens per CTA, 128 threads, 4 rows x 4 tokens per thread. The K loop runs
  * in 64-input chunks; within a chunk every accumulator is an fmaf chain in ascending k, and at the end of
  * the chunk it is added to the running total: exactly or_dot_f32's order. Chunks are double-buffered in
- * shared memory, stored k-major ([k][row], [k][token]) so each k step is two broadcast 16-byte loads. */
-constexpr int kGR = 64, kGT = 32;
+ * shared memory, stored k-major ([k][row], [k][token]) so each k step is two broadcast 16-byte loads.
+ * kSplit: the CTA (grid z) takes only kCG chunks and stores each chunk's chain value to
+ * part[chunk][t][row]; router_sum_kernel then adds the chunks in order (same order, 8x more CTAs). */
+constexpr int kGR = 64, kGT = 32, kCG = 2;
+template <bool kSplit>
 __global__ void __launch_bounds__(128) router_gemm_f32_kernel(const float *__restrict__ W,
                                                               const float *__restrict__ bias,
                                                               const float *__restrict__ x, int T, int H, int E,
-                                                              float *__restrict__ logits) {
+                                                              float *__restrict__ logits, float *__restrict__ part) {
     __shared__ __align__(16) float Ws[2][kChunk][kGR];   /* [buf][k][row]   */
     __shared__ __align__(16) float Xs[2][kChunk][kGT];   /* [buf][k][token] */
     const int tid = threadIdx.x, tx = tid & 7, ty = tid >> 3;
     const int r0 = blockIdx.x * kGR, t0 = blockIdx.y * kGT;
     const int Ep1 = E + 1;
-    const int nch = (H + kChunk - 1) / kChunk;
+    const int nch_all = (H + kChunk - 1) / kChunk;
+    const int cbeg = kSplit ? blockIdx.z * kCG : 0;
+    const int nch = kSplit ? min(nch_all, cbeg + kCG) : nch_all;   /* chunks [cbeg, nch) */
     /* loader mapping: W row = tid & 63, k quads (tid >> 6) + 2i (i < 8); X token = tid & 31, k quads
      * (tid >> 5) + 4i (i < 4). Consecutive lanes -> consecutive rows/tokens: conflict-free stores. */
     const int lr = tid & 63, lkq = tid >> 6, xr = tid & 31, xkq = tid >> 5;
@@ -126,52 +131,85 @@ __global__ void __launch_bounds__(128) router_gemm_f32_kernel(const float *__res
         }
     };
     float total[4][4], acc[4][4];
+    float2 acc2[4][2];   /* acc[i][2jj], acc[i][2jj+1] as pairs: independent chains in one paired fma */
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) total[i][j] = 0.0f;
-    load(0);
+    load(cbeg);
     store(0);
     __syncthreads();
-    for (int c = 0; c < nch; c++) {
-        const int b = c & 1;
+    for (int c = cbeg; c < nch; c++) {
+        const int b = (c - cbeg) & 1;
         if (c + 1 < nch) load(c + 1);
         const int kn = min(kChunk, H - c * kChunk);
 #pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        for (int i = 0; i < 4; i++) acc2[i][0] = acc2[i][1] = make_float2(0.0f, 0.0f);
 #pragma unroll 8
         for (int k = 0; k < kn; k++) {
             const float4 wv = *reinterpret_cast<const float4 *>(&Ws[b][k][ty * 4]);
             const float4 xv = *reinterpret_cast<const float4 *>(&Xs[b][k][tx * 4]);
             const float wr[4] = {wv.x, wv.y, wv.z, wv.w};
-            const float xr4[4] = {xv.x, xv.y, xv.z, xv.w};
+            const float2 x01 = make_float2(xv.x, xv.y), x23 = make_float2(xv.z, xv.w);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 w2 = make_float2(wr[i], wr[i]);
+                acc2[i][0] = __ffma2_rn(w2, x01, acc2[i][0]);
+                acc2[i][1] = __ffma2_rn(w2, x23, acc2[i][1]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            acc[i][0] = acc2[i][0].x; acc[i][1] = acc2[i][0].y;
+            acc[i][2] = acc2[i][1].x; acc[i][3] = acc2[i][1].y;
+        }
+        if constexpr (kSplit) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int r = r0 + ty * 4 + i;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int t = t0 + tx * 4 + j;
+                    if (r < Ep1 && t < T) part[((size_t)c * T + t) * Ep1 + r] = acc[i][j];
+                }
+            }
+        } else {
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(wr[i], xr4[j], acc[i][j]);
+                for (int j = 0; j < 4; j++) total[i][j] = __fadd_rn(total[i][j], acc[i][j]);
         }
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) total[i][j] = __fadd_rn(total[i][j], acc[i][j]);
         if (c + 1 < nch) store(b ^ 1);
         __syncthreads();
     }
+    if constexpr (!kSplit) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int r = r0 + ty * 4 + i;
-        if (r >= Ep1) continue;
+        for (int i = 0; i < 4; i++) {
+            const int r = r0 + ty * 4 + i;
+            if (r >= Ep1) continue;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int t = t0 + tx * 4 + j;
-            if (t >= T) continue;
-            float l = total[i][j];
-            if (bias && r < E) l = __fadd_rn(l, bias[r]);
-            logits[(size_t)t * Ep1 + r] = l;
+            for (int j = 0; j < 4; j++) {
+                const int t = t0 + tx * 4 + j;
+                if (t >= T) continue;
+                float l = total[i][j];
+                if (bias && r < E) l = __fadd_rn(l, bias[r]);
+                logits[(size_t)t * Ep1 + r] = l;
+            }
         }
     }
+}
+
+/* logits[t][r] = (((0 + part[0][t][r]) + part[1][t][r]) + ...) + bias[r]: or_dot_f32's chunk order. */
+__global__ void router_sum_kernel(const float *__restrict__ part, const float *__restrict__ bias, int nch, int T,
+                                  int E, float *__restrict__ logits) {
+    const int Ep1 = E + 1;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)T * Ep1) return;
+    const int r = (int)(i % Ep1);
+    float tot = 0.0f;
+    for (int c = 0; c < nch; c++) tot = __fadd_rn(tot, part[(size_t)c * T * Ep1 + i]);
+    if (bias && r < E) tot = __fadd_rn(tot, bias[r]);
+    logits[i] = tot;
 }
 
 /* Quantized router in qmat_matvec's exact order: one warp per (row, token); lane g owns groups g, g+32,
@@ -386,7 +424,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_topk_kernel(const floa
 }  // namespace
 
 int qe_launch_router_f32(const float *W, const float *bias, const float *x, int T, int H, int E, float *logits,
-                         cudaStream_t s) {
+                         float *part, cudaStream_t s) {
     if (H > 32 * kMaxLaneChunks * kChunk) QE_FAIL("router: hidden %d too large", H);
     if (T <= 16) {
         const int rows = E + 1, warps_per_block = 4;
@@ -394,8 +432,17 @@ int qe_launch_router_f32(const float *W, const float *bias, const float *x, int 
             W, bias, x, T, H, E, logits);
     } else {
         if (H % 4) QE_FAIL("router: hidden %d must be a multiple of 4", H);
-        dim3 grid((E + 1 + kGR - 1) / kGR, (T + kGT - 1) / kGT);
-        router_gemm_f32_kernel<<<grid, 128, 0, s>>>(W, bias, x, T, H, E, logits);
+        const int nch = (H + kChunk - 1) / kChunk;
+        if (part) {
+            dim3 grid((E + 1 + kGR - 1) / kGR, (T + kGT - 1) / kGT, (nch + kCG - 1) / kCG);
+            router_gemm_f32_kernel<true><<<grid, 128, 0, s>>>(W, bias, x, T, H, E, logits, part);
+            QE_CHECK(cudaGetLastError());
+            const long long n = (long long)T * (E + 1);
+            router_sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, bias, nch, T, E, logits);
+        } else {
+            dim3 grid((E + 1 + kGR - 1) / kGR, (T + kGT - 1) / kGT);
+            router_gemm_f32_kernel<false><<<grid, 128, 0, s>>>(W, bias, x, T, H, E, logits, nullptr);
+        }
     }
     QE_CHECK(cudaGetLastError());
     return 0;

@@ -29,6 +29,10 @@ namespace {
 constexpr int kNT = 8;       /* tokens per MMA (n8) */
 constexpr int kWarps = 4;    /* warps per CTA; each warp = 16 rows */
 constexpr int kRowsPerCta = 16 * kWarps;
+/* Decode-sized batches (T <= kSplitMaxT): the 4 warps of a CTA share 16 rows and split the groups of K
+ * between them (partials summed in warp order), so a 1-token step has 4x more CTAs streaming weights. */
+constexpr int kSplitMaxT = 4;
+constexpr int kSplitK = 4;
 
 enum { MODE_GATEUP = 0, MODE_DOWN = 1 };
 
@@ -139,30 +143,48 @@ __device__ void stage_rows(const float *const *rows, int nt, int K, uint32_t *xs
     }
 }
 
-/* One warp: out[4] (rows g, g+8 x tokens 2t, 2t+1) += W[16 rows] . x, full K. */
+/* One warp: out[4] (rows g, g+8 x tokens 2t, 2t+1) += W[16 rows] . x over groups [g0, g1), the range's
+ * group terms summed from 0 in group order and then added to out. The code words of the next kDepth
+ * groups are always in flight (a register ring), so a warp streams its rows instead of waiting one memory
+ * latency per group. */
+constexpr int kDepth = 4;
 template <int BITS, int GS, int NMAT>
 __device__ __forceinline__ void warp_qmm(const QeQDev *const mats[NMAT], const size_t row_word[NMAT][2],
-                                         const size_t row_grp[NMAT][2], size_t grp_stride, const bool row_ok[2], int ng,
-                                         const uint32_t *xs, const float *xsum, int tstride, int nt,
+                                         const size_t row_grp[NMAT][2], size_t grp_stride, const bool row_ok[2], int g0,
+                                         int g1, int ng, const uint32_t *xs, const float *xsum, int tstride, int nt,
                                          float (&acc)[NMAT][4]) {
     using G = Geo<BITS, GS>;
     const int lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
     const int lw = G::lane_word(t);
     const bool tok_ok = gq < nt;
     const uint32_t *xrow = xs + (size_t)gq * tstride + (size_t)t * G::S * 6;
-    for (int g = 0; g < ng; g++) {
-        Words<G::S> wa[NMAT][2];
+    float pacc[NMAT][4];
+#pragma unroll
+    for (int m = 0; m < NMAT; m++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) pacc[m][i] = 0.0f;
+    Words<G::S> ring[kDepth][NMAT][2];
+    auto fetch = [&](int g, Words<G::S>(&wa)[NMAT][2]) {
 #pragma unroll
         for (int m = 0; m < NMAT; m++)
 #pragma unroll
             for (int r = 0; r < 2; r++) {
-                if (row_ok[r]) {
+                if (row_ok[r] && g < g1) {
                     wa[m][r] = load_words<G::S>(mats[m]->w + row_word[m][r] + (size_t)g * G::WPG + lw);
                 } else {
 #pragma unroll
                     for (int i = 0; i < G::S; i++) wa[m][r].v[i] = 0u;
                 }
             }
+    };
+#pragma unroll
+    for (int d = 0; d < kDepth; d++) fetch(g0 + d, ring[d]);
+    for (int gb = g0; gb < g1; gb += kDepth)
+#pragma unroll
+    for (int d = 0; d < kDepth; d++) {
+        const int g = gb + d;
+        if (g >= g1) break;
+        Words<G::S>(&wa)[NMAT][2] = ring[d];
         float p[NMAT][4];
 #pragma unroll
         for (int m = 0; m < NMAT; m++)
@@ -202,10 +224,15 @@ __device__ __forceinline__ void warp_qmm(const QeQDev *const mats[NMAT], const s
                     sc = qe_bf16_to_f32(__ldg(mats[m]->scales + row_grp[m][r] + g * grp_stride));
                     bi = qe_bf16_to_f32(__ldg(mats[m]->biases + row_grp[m][r] + g * grp_stride));
                 }
-                acc[m][2 * r] = __fadd_rn(acc[m][2 * r], __fmaf_rn(sc, p[m][2 * r], __fmul_rn(bi, xs0)));
-                acc[m][2 * r + 1] = __fadd_rn(acc[m][2 * r + 1], __fmaf_rn(sc, p[m][2 * r + 1], __fmul_rn(bi, xs1)));
+                pacc[m][2 * r] = __fadd_rn(pacc[m][2 * r], __fmaf_rn(sc, p[m][2 * r], __fmul_rn(bi, xs0)));
+                pacc[m][2 * r + 1] = __fadd_rn(pacc[m][2 * r + 1], __fmaf_rn(sc, p[m][2 * r + 1], __fmul_rn(bi, xs1)));
             }
+        fetch(g + kDepth, ring[d]);
     }
+#pragma unroll
+    for (int m = 0; m < NMAT; m++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[m][i] = __fadd_rn(acc[m][i], pacc[m][i]);
 }
 
 __device__ __forceinline__ int find_slot(const int32_t *prefix, int n, int item) {
@@ -219,10 +246,12 @@ __device__ __forceinline__ int find_slot(const int32_t *prefix, int n, int item)
 
 /* MODE_GATEUP: h3[pair][row] = silu(gate.x) * (up.x)   (moe_layer.c:20-25, ops.c:16-21)
  * MODE_DOWN:   y[pair][row]  = down.h3                  (moe_layer.c:25) */
-template <int BITS, int GS, int MODE>
+template <int BITS, int GS, int MODE, int KS>
 __global__ void __launch_bounds__(kWarps * 32) expert_kernel(QeExpertArgs a, const float *__restrict__ xin, int ldx,
                                                              QeBuckets bk, int T, float *__restrict__ out,
                                                              int ldo, int chunk) {
+    constexpr int kRows = 16 * kWarps / KS;   /* rows per CTA */
+    __shared__ float red[KS > 1 ? kWarps * 32 * 8 : 1];
     extern __shared__ __align__(16) uint32_t smem[];
     using G = Geo<BITS, GS>;
     const int Kmax = MODE == MODE_GATEUP ? a.hidden : max(a.inter, a.sh_inter);
@@ -243,7 +272,7 @@ __global__ void __launch_bounds__(kWarps * 32) expert_kernel(QeExpertArgs a, con
         const int count = bk.counts[e], off = bk.offsets[e];
         const int rows_total = MODE == MODE_GATEUP ? (shared ? a.sh_inter : a.inter) : a.hidden;
         const int K = MODE == MODE_GATEUP ? a.hidden : (shared ? a.sh_inter : a.inter);
-        const int tiles = (rows_total + kRowsPerCta - 1) / kRowsPerCta;
+        const int tiles = (rows_total + kRows - 1) / kRows;
         const int local = item - prefix[slot];
         const int ch = local / tiles, tile = local % tiles;
         const int p0 = ch * chunk;
@@ -263,8 +292,22 @@ __global__ void __launch_bounds__(kWarps * 32) expert_kernel(QeExpertArgs a, con
         __syncthreads();
         stage_rows<BITS, GS>(rows, nt, K, xs, xsum, tstride);
         __syncthreads();
-        const int r_base = tile * kRowsPerCta + warp * 16;
+        const int sub = warp / KS, part = warp % KS;
+        const int r_base = tile * kRows + sub * 16;
         const int ng = K / GS;
+        /* the group ranges of the decode split; a warp that owns all of them runs them in order, so a token's
+         * sums are the same whichever kernel variant (batch size) computes them */
+        const int q0 = KS > 1 ? part : 0, q1 = KS > 1 ? part + 1 : kSplitK;
+        /* KS > 1: the warps of a row block add their partials in warp order into the first one */
+        auto reduce_parts = [&](float *accv, int n) {
+            if constexpr (KS > 1) {
+                for (int i = 0; i < n; i++) red[(warp * 32 + lane) * 8 + i] = accv[i];
+                __syncthreads();
+                if (part == 0)
+                    for (int q = 1; q < KS; q++)
+                        for (int i = 0; i < n; i++) accv[i] = __fadd_rn(accv[i], red[((warp + q) * 32 + lane) * 8 + i]);
+            }
+        };
         const bool row_ok[2] = {r_base + gq < rows_total, r_base + gq + 8 < rows_total};
         if (MODE == MODE_GATEUP) {
             const QeQDev *mats[2] = {shared ? &a.sh_gate : &a.gate, shared ? &a.sh_up : &a.up};
@@ -281,14 +324,16 @@ __global__ void __launch_bounds__(kWarps * 32) expert_kernel(QeExpertArgs a, con
                     rg[m][r] = mats[m]->scale_t ? eg * gpr * rows_total + rin : (ebase + rin) * gpr;
                 }
             float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
-            warp_qmm<BITS, GS, 2>(mats, rw, rg, mats[0]->scale_t ? (size_t)rows_total : 1, row_ok, ng, xs, xsum,
-                                  tstride, nt, acc);
+            for (int q = q0; q < q1; q++)
+                warp_qmm<BITS, GS, 2>(mats, rw, rg, mats[0]->scale_t ? (size_t)rows_total : 1, row_ok,
+                                      q * ng / kSplitK, (q + 1) * ng / kSplitK, ng, xs, xsum, tstride, nt, acc);
+            reduce_parts(&acc[0][0], 8);
 #pragma unroll
             for (int r = 0; r < 2; r++)
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     const int n = 2 * t + c;
-                    if (row_ok[r] && n < nt) {
+                    if (part == 0 && row_ok[r] && n < nt) {
                         const int row = r_base + gq + 8 * r;
                         out[(size_t)pair_ids[n] * ldo + row] = qe_silu_mul(acc[0][2 * r + c], acc[1][2 * r + c]);
                     }
@@ -306,14 +351,16 @@ __global__ void __launch_bounds__(kWarps * 32) expert_kernel(QeExpertArgs a, con
                 rg[0][r] = mats[0]->scale_t ? eg * gpr * rows_total + rin : (ebase + rin) * gpr;
             }
             float acc[1][4] = {{0, 0, 0, 0}};
-            warp_qmm<BITS, GS, 1>(mats, rw, rg, mats[0]->scale_t ? (size_t)rows_total : 1, row_ok, ng, xs, xsum,
-                                  tstride, nt, acc);
+            for (int q = q0; q < q1; q++)
+                warp_qmm<BITS, GS, 1>(mats, rw, rg, mats[0]->scale_t ? (size_t)rows_total : 1, row_ok,
+                                      q * ng / kSplitK, (q + 1) * ng / kSplitK, ng, xs, xsum, tstride, nt, acc);
+            reduce_parts(&acc[0][0], 4);
 #pragma unroll
             for (int r = 0; r < 2; r++)
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     const int n = 2 * t + c;
-                    if (row_ok[r] && n < nt) {
+                    if (part == 0 && row_ok[r] && n < nt) {
                         const int row = r_base + gq + 8 * r;
                         out[(size_t)pair_ids[n] * ldo + row] = acc[0][2 * r + c];
                     }
@@ -331,7 +378,7 @@ int launch_expert(const QeExpertArgs *a, const float *xin, int ldx, const QeBuck
     const int chunk = T < kNT ? T : kNT;
     const size_t smem = sizeof(uint32_t) * (size_t)chunk * tstride + sizeof(float) * (size_t)kNT * (Kmax / GS);
     if (smem > 200 * 1024) QE_FAIL("expert kernel: K=%d needs %zu B of shared memory", Kmax, smem);
-    auto kern = expert_kernel<BITS, GS, MODE>;
+    auto kern = T <= kSplitMaxT ? expert_kernel<BITS, GS, MODE, kSplitK> : expert_kernel<BITS, GS, MODE, 1>;
     QE_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     kern<<<grid, kWarps * 32, smem, s>>>(*a, xin, ldx, *b, T, out, ldo, chunk);
     QE_CHECK(cudaGetLastError());
@@ -415,7 +462,8 @@ __global__ void __launch_bounds__(kWarps * 32) qmat_kernel(QeQDev m, const float
         rg[0][r] = m.scale_t ? row : row * gpr;
     }
     float acc[1][4] = {{0, 0, 0, 0}};
-    warp_qmm<BITS, GS, 1>(mats, rw, rg, m.scale_t ? (size_t)m.rows : 1, row_ok, ng, xs, xsum, tstride, nt, acc);
+    warp_qmm<BITS, GS, 1>(mats, rw, rg, m.scale_t ? (size_t)m.rows : 1, row_ok, 0, ng, ng, xs, xsum, tstride, nt,
+                          acc);
 #pragma unroll
     for (int r = 0; r < 2; r++)
 #pragma unroll
@@ -469,7 +517,7 @@ int qe_launch_combine_sel(const float *ybuf, const int32_t *idx, const float *sc
     return 0;
 }
 
-int qe_expert_rows_per_cta(void) { return kRowsPerCta; }
+int qe_expert_rows_per_cta(int T) { return T <= kSplitMaxT ? kRowsPerCta / kSplitK : kRowsPerCta; }
 
 int qe_launch_qmatvec(const QeQDev *m, const float *x, int T, float *y, cudaStream_t s) {
     const int bits = m->bits, gs = m->group_size;

@@ -23,7 +23,7 @@
 #include "synth.h"
 #include "../../include/qe_moe.h"
 
-int qe_expert_rows_per_cta(void);
+int qe_expert_rows_per_cta(int T);
 
 /* Batches of at least this many tokens take the tensor-core (tcgen05) expert path when the shape allows. */
 static constexpr int kTcMinTokens = 64;
@@ -518,7 +518,7 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
         g_launches += 5;
         return 0;
     }
-    const int R = qe_expert_rows_per_cta();
+    const int R = qe_expert_rows_per_cta(T);
     const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R, tiles_dn = (c.hidden + R - 1) / R;
     const int chunk = T < 8 ? T : 8;
     if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, tiles_gu, tiles_sh, tiles_dn, chunk, &sc.b, s)) return -1;
@@ -661,7 +661,7 @@ int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sm
             return -1;
         g_launches += 4;
     } else {
-        const int R = qe_expert_rows_per_cta();
+        const int R = qe_expert_rows_per_cta(n);
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
                   tiles_dn = (c.hidden + R - 1) / R;
         const int chunk = n < 8 ? n : 8;

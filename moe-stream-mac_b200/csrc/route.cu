@@ -19,11 +19,12 @@ constexpr int kGemvTokens = 8;
 
 /* Decode / small batch: one warp per router row (E routed rows + the shared gate row). Lane c owns
  * chunks c, c+32, ...; each chunk is an fmaf chain per token; lane 0..nt-1 then add the chunk sums in
- * chunk order. */
+ * chunk order. vec (W, x 16-byte aligned, H % 4 == 0): a lane requests its whole 64-float weight chunk
+ * with 16-byte loads before the chain starts. */
 __global__ void __launch_bounds__(128) router_gemv_f32_kernel(const float *__restrict__ W,
                                                               const float *__restrict__ bias,
                                                               const float *__restrict__ x, int T, int H, int E,
-                                                              float *__restrict__ logits) {
+                                                              float *__restrict__ logits, int vec) {
     const int lane = threadIdx.x & 31;
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (row > E) return;
@@ -38,7 +39,27 @@ __global__ void __launch_bounds__(128) router_gemv_f32_kernel(const float *__res
 #pragma unroll
             for (int t = 0; t < kGemvTokens; t++) acc[cc][t] = 0.0f;
             const int c = lane + 32 * cc;
-            if (c < nch) {
+            if (c < nch && vec && (c + 1) * kChunk <= H) {
+                const float4 *w4 = reinterpret_cast<const float4 *>(w + (size_t)c * kChunk);
+                float4 wv[kChunk / 4];
+#pragma unroll
+                for (int q = 0; q < kChunk / 4; q++) wv[q] = __ldg(w4 + q);
+#pragma unroll
+                for (int t = 0; t < kGemvTokens; t++) {
+                    if (t >= nt) break;
+                    const float4 *x4 = reinterpret_cast<const float4 *>(x + (size_t)(t0 + t) * H + (size_t)c * kChunk);
+                    float a = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < kChunk / 4; q++) {
+                        const float4 xv = __ldg(x4 + q);
+                        a = __fmaf_rn(wv[q].x, xv.x, a);
+                        a = __fmaf_rn(wv[q].y, xv.y, a);
+                        a = __fmaf_rn(wv[q].z, xv.z, a);
+                        a = __fmaf_rn(wv[q].w, xv.w, a);
+                    }
+                    acc[cc][t] = a;
+                }
+            } else if (c < nch) {
                 const int i0 = c * kChunk, i1 = min(i0 + kChunk, H);
                 for (int i = i0; i < i1; i++) {
                     const float wv = __ldg(w + i);
@@ -428,8 +449,9 @@ int qe_launch_router_f32(const float *W, const float *bias, const float *x, int 
     if (H > 32 * kMaxLaneChunks * kChunk) QE_FAIL("router: hidden %d too large", H);
     if (T <= 16) {
         const int rows = E + 1, warps_per_block = 4;
+        const int vec = H % 4 == 0 && ((uintptr_t)W | (uintptr_t)x) % 16 == 0;
         router_gemv_f32_kernel<<<(rows + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, s>>>(
-            W, bias, x, T, H, E, logits);
+            W, bias, x, T, H, E, logits, vec);
     } else {
         if (H % 4) QE_FAIL("router: hidden %d must be a multiple of 4", H);
         const int nch = (H + kChunk - 1) / kChunk;

@@ -71,6 +71,19 @@ QeMoe *qe_moe_create(const QeMoeConfig *cfg, const QeMoeWeights *w);
  * CPU checker's copy). router_bias: [E] host array or NULL. */
 QeMoe *qe_moe_create_synthetic(const QeMoeConfig *cfg, uint64_t seed, uint32_t block, const float *router_bias);
 
+/* The block of one layer from an MLX checkpoint directory (every *.safetensors shard in `dir`), as the
+ * reference's load_moe reads it (engine/src/model.c:52-70, engine/src/loader.c:16-41,
+ * engine/src/io/k3_st.c:509): tensors <prefix>.switch_mlp.{gate,up,down}_proj, <prefix>.gate,
+ * <prefix>.shared_expert.{gate,up,down}_proj, <prefix>.shared_expert_gate, each .weight/.scales/.biases.
+ * prefix is e.g. "language_model.model.layers.3.mlp". From cfg only top_k, group_size, max_tokens, device,
+ * layer and ep_rank/ep_size are taken; hidden, E, inter, sh_inter, bits and the quantized router's bits come
+ * from the tensor shapes (a nonzero cfg value that disagrees is refused). NULL on failure (stderr says why). */
+QeMoe *qe_moe_open_safetensors(const char *dir, const char *prefix, const QeMoeConfig *cfg);
+
+/* dtype (e.g. "U32", NUL-terminated, <= 7 chars) and shape[ndim] (ndim <= 8) of one tensor of a checkpoint
+ * directory; host only, no GPU needed. 0 ok, -1 if missing or malformed. */
+int qe_safetensors_tensor_info(const char *dir, const char *name, char *dtype, int64_t *shape, int *ndim);
+
 void qe_moe_free(QeMoe *m);
 
 /* out[T][hidden] = moe(x[T][hidden]) for T >= 1 independent tokens, host buffers (x, out may not alias).

@@ -65,6 +65,24 @@ class MoeBlock:
         if not self.handle:
             raise EngineError("qe_moe_create failed (see the message above)")
 
+    @classmethod
+    def from_safetensors(cls, directory: str, prefix: str, top_k: int, group_size: int = 64, *, max_tokens: int = 4096,
+                         device: int = 0, layer: int = 0, ep_rank: int = 0, ep_size: int = 1) -> "MoeBlock":
+        """One layer's block from an MLX checkpoint directory (qe_moe_open_safetensors): the shapes come
+        from the tensors, e.g. prefix="language_model.model.layers.3.mlp"."""
+        self = cls.__new__(cls)
+        self.cfg = QeMoeConfig(0, 0, top_k, 0, 0, 0, group_size, QE_ROUTER_QMAT, 0, max_tokens, device, layer,
+                               ep_rank, ep_size)
+        self.ep_rank, self.ep_size = ep_rank, ep_size
+        self._keep = []
+        self.handle = lib().qe_moe_open_safetensors(str(directory).encode(), prefix.encode(), C.byref(self.cfg))
+        if not self.handle:
+            raise EngineError("qe_moe_open_safetensors failed (see the message above)")
+        L = lib()
+        self.hidden, self.top_k = L.qe_moe_hidden(self.handle), top_k
+        self.E = None
+        return self
+
     def close(self) -> None:
         if getattr(self, "handle", None):
             lib().qe_moe_free(self.handle)

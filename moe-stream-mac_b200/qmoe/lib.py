@@ -76,6 +76,10 @@ def lib() -> C.CDLL:
         L.qe_moe_ep_experts_device.argtypes = [vp, C.c_int, vp, vp, vp, vp]
         L.qe_moe_ep_combine_device.argtypes = [vp, C.c_int, vp, vp, vp, vp, vp]
         L.qe_moe_ep_size.argtypes = [vp]
+        L.qe_moe_open_safetensors.restype = vp
+        L.qe_moe_open_safetensors.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(QeMoeConfig)]
+        L.qe_safetensors_tensor_info.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(C.c_int64),
+                                                 C.POINTER(C.c_int)]
         _lib = L
     return _lib
 
@@ -162,3 +166,13 @@ def kernel_launches() -> int:
 
 def device_count() -> int:
     return lib().qe_device_count()
+
+
+def safetensors_tensor_info(directory: str, name: str):
+    """(dtype, shape) of one tensor of a checkpoint directory, parsed by the library (no GPU needed)."""
+    dt = C.create_string_buffer(8)
+    shape = (C.c_int64 * 8)()
+    nd = C.c_int(0)
+    if lib().qe_safetensors_tensor_info(str(directory).encode(), name.encode(), dt, shape, C.byref(nd)):
+        raise KeyError(name)
+    return dt.value.decode(), tuple(shape[i] for i in range(nd.value))

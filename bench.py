@@ -155,13 +155,13 @@ def run_reference_arm(args, cfg):
     print(json.dumps(line))
 
 
-def workload_config(cfg, world, blocks=4):
+def workload_config(cfg, world, blocks=4, ep_mode="rows and partial sums stored into peer memory by the kernels"):
     mb = blocks * (cfg.E // world * cfg.expert_bytes + cfg.shared_bytes + 4 * cfg.E * cfg.hidden) / 1e6
     return {"workload": f"{cfg.name}: {cfg.note}", "tokens_per_step": cfg.tokens, "hidden": cfg.hidden,
             "experts": cfg.E, "top_k": cfg.top_k, "inter": cfg.inter, "sh_inter": cfg.sh_inter, "bits": cfg.bits,
             "group_size": cfg.group_size, "router": "fp32", "parallelism": "1 GPU" if world == 1 else
             f"expert parallel over {world} GPUs ({cfg.E // world} experts each; router and shared expert "
-            f"replicated; {cfg.tokens} tokens per GPU; all_to_all over NCCL)",
+            f"replicated; {cfg.tokens} tokens per GPU; exchange: {ep_mode})",
             "l2": f"{blocks} blocks with distinct weights rotated per step ({mb:.0f} MB of weights per GPU > 126 MB L2)"}
 
 
@@ -202,7 +202,7 @@ def stage_bytes(cfg, uniq: int, T: int) -> dict:
     return {"gateup": gu, "down": dn}
 
 
-def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, nprof=10):
+def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, mode, nprof=10):
     """Per-phase times of the expert-parallel step (CUDA events between phases, a separate run after the
     timed region) and the roofline of its expert stage: this rank's touched experts' weights once, plus the
     rows it receives and the partial sums it returns."""
@@ -218,7 +218,7 @@ def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, nprof=10
             ev = torch.cuda.Event(enable_timing=True)
             ev.record(stream)
             evs.append((name, ev))
-        models[i % len(models)].forward(x, mark=mark)
+        models[i % len(models)].forward(x, mode=mode, mark=mark)
         torch.cuda.synchronize()
         prev = e_start
         for name, ev in evs:
@@ -261,6 +261,8 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=16)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-mode", default="p2p", choices=["p2p", "sharded"],
+                    help="N > 1: exchange through peer memory (p2p) or NCCL all_to_all (sharded)")
     args = ap.parse_args()
 
     from qmoe.synth import CONFIGS
@@ -288,10 +290,13 @@ def main():
         from qmoe.ep import ExpertParallelMoe
         models = [ExpertParallelMoe.on_gpu(cfg, rank, world, local, seed=b + 1, block=b, max_tokens=world * T)
                   for b in range(args.blocks)]
+        if args.ep_mode == "p2p":
+            for mdl in models:
+                mdl.enable_p2p(T)
         blocks = [m.engine.block for m in models]
 
         def step(i):
-            models[i % len(models)].forward(x)
+            models[i % len(models)].forward(x, mode=args.ep_mode)
     else:
         blocks = [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size,
                                 max_tokens=T, device=local, seed=b + 1, block=b) for b in range(args.blocks)]
@@ -339,7 +344,7 @@ def main():
     def e2e_step(i):
         if ep:   # qmoe.ep.ExpertParallelMoe.forward with the copies in and out of pinned host memory
             xd = xh.to("cuda", non_blocking=True)
-            oh.copy_(models[i % len(models)].forward(xd), non_blocking=True)
+            oh.copy_(models[i % len(models)].forward(xd, mode=args.ep_mode), non_blocking=True)
             torch.cuda.current_stream().synchronize()
         else:    # qe_moe_forward: host buffers in and out
             blocks[i % len(blocks)].forward(xn, on)
@@ -360,7 +365,7 @@ def main():
     peak, peak_kind = hbm_peak()
     peak_source = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s")
     if ep:
-        roofline = ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source)
+        roofline = ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, args.ep_mode)
     else:
         # roofline of the dominant kernel (per-stage CUDA events recorded inside the timed region)
         idx, _ = blocks[0].route(x.cpu().numpy())
@@ -384,13 +389,17 @@ def main():
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(cfg, world, args.blocks),
+            "config": workload_config(cfg, world, args.blocks, "rows and partial sums stored into peer memory by the "
+                                      "kernels" if args.ep_mode == "p2p" else "all_to_all over NCCL"),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * cfg.hidden,
                     "d2h_bytes_per_step": 4 * T * cfg.hidden, "steps": ke, "timing": "host clock, max over ranks"},
             "roofline": roofline, "gpu_launches": launches, "clocks": clk}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = time_reference(cfg, 1, args.ref_tokens, 1000, 1, os.cpu_count() or 1, budget_s=args.cpu_budget)
         line["cpu_baseline"] = cb if cb else {"value": None, "unavailable": "oracle/_ref missing"}
+    if ep:
+        for mdl in models:
+            mdl.close()
     for b in blocks:
         b.close()
     if world > 1:

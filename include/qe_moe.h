@@ -127,6 +127,34 @@ int qe_moe_ep_combine_device(QeMoe *m, int T, const float *part, const int32_t *
                              void *stream);
 int qe_moe_ep_size(const QeMoe *m);
 
+/* Token-sharded step with the exchange done by the kernels themselves through peer memory (NVLink stores
+ * into CUDA-IPC mappings of the other ranks' buffers), instead of two all_to_all calls:
+ *   qe_ep_xchg_create        this rank's receive and return buffers for steps of up to T_max tokens per rank
+ *                            (rows [G][T_max][h], slot lists [G][T_max][2k], partial rows [G][T_max][h]);
+ *                            writes its qe_ep_xchg_handle_bytes()-byte IPC handle to `handle`
+ *   qe_ep_xchg_connect       handles[G][handle bytes] of every rank (own entry ignored): map the peers
+ *   qe_ep_xchg_connect_local ranks emulated in one process on one device (tests): n contexts, plain pointers
+ * Per step, after qe_moe_ep_route_device:
+ *   qe_moe_ep_dispatch_p2p   plan (home, counts as qe_moe_ep_pack_device) and write each row and slot list
+ *                            into its destination rank's receive buffer (block = this rank, padded to T rows)
+ *   (caller) a barrier across the ranks on the stream, e.g. a one-element all_reduce
+ *   qe_moe_ep_experts_p2p    the expert stage on the G*T received rows, each partial row written into its
+ *                            home rank's return buffer
+ *   (caller) a barrier across the ranks on the stream
+ *   qe_moe_ep_combine_p2p    out[t] = sum over ranks d ascending of return[d][home[d][t]] + shared[t]
+ * Same arithmetic as the all_to_all step (bit-identical results). No multicast, only plain loads and stores. */
+typedef struct QeEpXchg QeEpXchg;
+QeEpXchg *qe_ep_xchg_create(QeMoe *m, int T_max, void *handle);
+int qe_ep_xchg_handle_bytes(void);
+int qe_ep_xchg_connect(QeEpXchg *x, const void *handles);
+int qe_ep_xchg_connect_local(QeEpXchg *const *all, int n);
+void qe_ep_xchg_free(QeEpXchg *x);
+int qe_moe_ep_dispatch_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, const int32_t *meta, int32_t *home,
+                           int32_t *counts, void *stream);
+int qe_moe_ep_experts_p2p(QeMoe *m, QeEpXchg *xc, int T, void *stream);
+int qe_moe_ep_combine_p2p(QeMoe *m, QeEpXchg *xc, int T, const int32_t *home, const float *shared, float *out,
+                          void *stream);
+
 /* Block accessors. */
 int qe_moe_hidden(const QeMoe *m);
 int qe_moe_top_k(const QeMoe *m);

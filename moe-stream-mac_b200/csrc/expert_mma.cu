@@ -517,6 +517,36 @@ int qe_launch_combine_sel(const float *ybuf, const int32_t *idx, const float *sc
     return 0;
 }
 
+/* Expert parallelism through peer memory: the same partial sums as combine_sel_kernel (routed slots only),
+ * each row written straight into its home rank's return buffer. Row t (global row row0 + t of the receive
+ * buffer) came from rank s = (row0 + t) / Tblk, slot (row0 + t) % Tblk; it lands at
+ * dst_base[s] + (self * Tblk + slot) * H. Rows without a slot of this rank are padding and are skipped. */
+__global__ void combine_sel_scatter_kernel(const float *__restrict__ ybuf, const int32_t *__restrict__ idx,
+                                           const float *__restrict__ score, int T, int k, int H,
+                                           float *const *__restrict__ dst_base, int row0, int Tblk, int self) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)T * H) return;
+    const int t = (int)(i / H), j = (int)(i % H);
+    bool any = false;
+    for (int s = 0; s < k; s++) any |= idx[(size_t)t * k + s] >= 0;
+    if (!any) return;
+    const float *y = ybuf + (size_t)t * (k + 1) * H + j;
+    float o = 0.0f;
+    for (int s = 0; s < k; s++)
+        if (idx[(size_t)t * k + s] >= 0) o = __fadd_rn(o, __fmul_rn(score[(size_t)t * k + s], y[(size_t)s * H]));
+    const int r = row0 + t, src = r / Tblk, slot = r % Tblk;
+    dst_base[src][((size_t)self * Tblk + slot) * H + j] = o;
+}
+
+int qe_launch_combine_sel_scatter(const float *ybuf, const int32_t *idx, const float *score, int T, int k, int H,
+                                  float *const *dst_base, int row0, int Tblk, int self, cudaStream_t s) {
+    const long long n = (long long)T * H;
+    combine_sel_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ybuf, idx, score, T, k, H, dst_base, row0,
+                                                                           Tblk, self);
+    QE_CHECK(cudaGetLastError());
+    return 0;
+}
+
 int qe_expert_rows_per_cta(int T) { return T <= kSplitMaxT ? kRowsPerCta / kSplitK : kRowsPerCta; }
 
 int qe_launch_qmatvec(const QeQDev *m, const float *x, int T, float *y, cudaStream_t s) {

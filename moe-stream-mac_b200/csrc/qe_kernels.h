@@ -56,6 +56,10 @@ int qe_launch_combine_sel(const float *ybuf, const int32_t *idx, const float *sc
                           int ld_logits, int T, int E, int k, int H, int with_routed, int with_shared, float *out,
                           cudaStream_t s);
 
+int qe_launch_combine_sel_scatter(const float *ybuf, const int32_t *idx, const float *score, int T, int k, int H,
+                                  float *const *dst_base /* device [G] */, int row0, int Tblk, int self,
+                                  cudaStream_t s);
+
 /* Generic quantized matrix-vector products (engine/src/qmat.c:15-49 semantics) over T vectors. */
 int qe_launch_qmatvec(const QeQDev *m, const float *x, int T, float *y, cudaStream_t s);
 

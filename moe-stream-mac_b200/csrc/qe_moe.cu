@@ -642,10 +642,17 @@ __global__ void ep_combine_kernel(const float *__restrict__ part, const int32_t 
     out[i] = __fadd_rn(o, shared[i]);
 }
 
+/* Where the expert stage's partial rows go when they are written into the home ranks' return buffers. */
+struct EpScatter {
+    float *const *base;   /* device [G]: every rank's return buffer */
+    int row0, Tblk, self;
+};
+
 /* The expert stages for n rows whose local slot ids and scores are in sc.idx / sc.score (and, for the shared
- * expert, whose gate logits are in sc.logits): bucket, gate/up + SwiGLU, down, then the selective combine. */
+ * expert, whose gate logits are in sc.logits): bucket, gate/up + SwiGLU, down, then the selective combine
+ * into out[n][hidden], or (scatter) into the home ranks' return buffers. */
 int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sms, bool routed, bool shared,
-                cudaStream_t s) {
+                cudaStream_t s, const EpScatter *scatter = nullptr) {
     const QeMoeConfig &c = m->cfg;
     const int El = m->E_loc, k = c.top_k;
     const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
@@ -676,11 +683,41 @@ int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sm
             return -1;
         g_launches += 3;
     }
-    if (qe_launch_combine_sel(sc.ybuf, sc.idx, sc.score, sc.logits, c.E + 1, n, c.E, k, c.hidden, routed ? 1 : 0,
-                              shared ? 1 : 0, out, s))
+    if (scatter) {
+        if (qe_launch_combine_sel_scatter(sc.ybuf, sc.idx, sc.score, n, k, c.hidden, scatter->base, scatter->row0,
+                                          scatter->Tblk, scatter->self, s))
+            return -1;
+    } else if (qe_launch_combine_sel(sc.ybuf, sc.idx, sc.score, sc.logits, c.E + 1, n, c.E, k, c.hidden,
+                                     routed ? 1 : 0, shared ? 1 : 0, out, s)) {
         return -1;
+    }
     g_launches += 1;
     return 0;
+}
+
+/* Warp (d, t), peer-memory dispatch: token t's row and slot list go straight into rank d's receive buffers,
+ * block `self`, row home[d][t]; row t of that block at or past counts[d] becomes padding. */
+__global__ void ep_scatter_p2p_kernel(const float *__restrict__ x, const int32_t *__restrict__ meta, int T, int H,
+                                      int k, int G, int self, const int32_t *__restrict__ home,
+                                      const int32_t *__restrict__ counts, float *const *__restrict__ recv_x,
+                                      int32_t *const *__restrict__ recv_meta) {
+    const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= (long long)G * T) return;
+    const int d = (int)(w / T), t = (int)(w % T);
+    const int pos = home[(size_t)d * T + t];
+    if (pos >= 0) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * H);
+        float4 *dst = reinterpret_cast<float4 *>(recv_x[d] + ((size_t)self * T + pos) * H);
+        for (int c = lane; c < H / 4; c += 32) dst[c] = src[c];
+        int32_t *dm = recv_meta[d] + ((size_t)self * T + pos) * 2 * k;
+        for (int c = lane; c < 2 * k; c += 32) dm[c] = meta[(size_t)t * 2 * k + c];
+    }
+    if (t >= counts[d]) {
+        int32_t *dm = recv_meta[d] + ((size_t)self * T + t) * 2 * k;
+        for (int c = lane; c < 2 * k; c += 32) dm[c] = c < k ? -1 : 0;
+    }
+    __threadfence_system();
 }
 
 void trace_route(const QeMoe *m, const int32_t *idx, int T) {
@@ -860,6 +897,164 @@ int qe_moe_ep_combine_device(QeMoe *m, int T, const float *part, const int32_t *
     QE_CHECK(cudaGetLastError());
     g_launches += 1;
     return 0;
+}
+
+/* ---- expert-parallel exchange through peer memory (CUDA IPC mappings of every rank's buffers) ---- */
+
+}  // extern "C"
+
+struct QeEpXchg {
+    QeMoe *m;
+    int G, self, Tmax, H, k;
+    char *mine;                      /* this rank's buffers: recv_x [G][Tmax][H], recv_meta [G][Tmax][2k], back [G][Tmax][H] */
+    size_t off_meta, off_back, bytes;
+    char *base[64];                  /* every rank's allocation as mapped here (own = mine)                      */
+    bool opened[64];
+    void **dptr;                     /* device arrays: recv_x[G], recv_meta[G], back[G]                          */
+    int T;                           /* tokens per rank of the current step                                     */
+};
+
+namespace {
+/* The three buffers are laid out for the step's T (blocks of T rows), within the Tmax capacity. */
+void xchg_tables(QeEpXchg *x, int T, void **host) {
+    for (int r = 0; r < x->G; r++) {
+        char *b = x->base[r];
+        host[r] = b;
+        host[x->G + r] = b + x->off_meta;
+        host[2 * x->G + r] = b + x->off_back;
+    }
+    (void)T;
+}
+}  // namespace
+
+extern "C" {
+
+QeEpXchg *qe_ep_xchg_create(QeMoe *m, int T_max, void *handle) {
+    if (!m || T_max < 1 || !handle) {
+        fprintf(stderr, "qengine_b200: ep_xchg_create: bad arguments\n");
+        return nullptr;
+    }
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return nullptr;
+    QeEpXchg *x = (QeEpXchg *)calloc(1, sizeof(QeEpXchg));
+    if (!x) return nullptr;
+    x->m = m;
+    x->G = m->cfg.ep_size;
+    x->self = m->cfg.ep_rank;
+    x->Tmax = T_max;
+    x->H = m->cfg.hidden;
+    x->k = m->cfg.top_k;
+    const size_t rows = (size_t)x->G * T_max;
+    x->off_meta = align256(rows * x->H * 4);
+    x->off_back = x->off_meta + align256(rows * 2 * x->k * 4);
+    x->bytes = x->off_back + align256(rows * x->H * 4);
+    if (cudaMalloc((void **)&x->mine, x->bytes) != cudaSuccess ||
+        cudaMalloc((void **)&x->dptr, sizeof(void *) * 3 * x->G) != cudaSuccess ||
+        cudaIpcGetMemHandle((cudaIpcMemHandle_t *)handle, x->mine) != cudaSuccess) {
+        fprintf(stderr, "qengine_b200: ep_xchg_create: cannot allocate or export %zu bytes\n", x->bytes);
+        if (x->mine) cudaFree(x->mine);
+        if (x->dptr) cudaFree(x->dptr);
+        free(x);
+        return nullptr;
+    }
+    x->base[x->self] = x->mine;
+    return x;
+}
+
+int qe_ep_xchg_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+int qe_ep_xchg_connect(QeEpXchg *x, const void *handles) {
+    if (!x || !handles) QE_FAIL("ep_xchg_connect: bad arguments");
+    QE_CHECK(cudaSetDevice(x->m->device));
+    for (int r = 0; r < x->G; r++) {
+        if (r == x->self || x->opened[r]) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const char *)handles + (size_t)r * sizeof(h), sizeof(h));
+        void *p = nullptr;
+        QE_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        x->base[r] = (char *)p;
+        x->opened[r] = true;
+    }
+    void *host[3 * 64];
+    xchg_tables(x, 0, host);
+    QE_CHECK(cudaMemcpy(x->dptr, host, sizeof(void *) * 3 * x->G, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+int qe_ep_xchg_connect_local(QeEpXchg *const *all, int n) {
+    /* ranks emulated in one process on one device: the buffers are plain device pointers */
+    if (!all || n < 1) QE_FAIL("ep_xchg_connect_local: bad arguments");
+    for (int i = 0; i < n; i++) {
+        QeEpXchg *x = all[i];
+        if (!x || x->G != n) QE_FAIL("ep_xchg_connect_local: %d contexts for ep_size %d", n, x ? x->G : -1);
+        for (int r = 0; r < n; r++) x->base[r] = all[r]->mine;
+        void *host[3 * 64];
+        xchg_tables(x, 0, host);
+        QE_CHECK(cudaSetDevice(x->m->device));
+        QE_CHECK(cudaMemcpy(x->dptr, host, sizeof(void *) * 3 * x->G, cudaMemcpyHostToDevice));
+    }
+    return 0;
+}
+
+void qe_ep_xchg_free(QeEpXchg *x) {
+    if (!x) return;
+    cudaSetDevice(x->m->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < x->G; r++)
+        if (x->opened[r]) cudaIpcCloseMemHandle(x->base[r]);
+    cudaFree(x->dptr);
+    cudaFree(x->mine);
+    free(x);
+}
+
+int qe_moe_ep_dispatch_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, const int32_t *meta, int32_t *home,
+                           int32_t *counts, void *stream) {
+    if (!m || !xc || !x || !meta || !home || !counts || T < 1 || T > xc->Tmax) QE_FAIL("ep_dispatch_p2p: bad arguments");
+    const int H = m->cfg.hidden, k = m->cfg.top_k, G = m->cfg.ep_size;
+    if (H % 4 || (uintptr_t)x % 16) QE_FAIL("ep_dispatch_p2p: x must be 16-byte aligned");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = (cudaStream_t)stream;
+    ep_plan_kernel<<<G, 1024, 0, s>>>(meta, T, k, m->E_loc, home, counts);
+    QE_CHECK(cudaGetLastError());
+    const long long threads = (long long)G * T * 32;
+    ep_scatter_p2p_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+        x, meta, T, H, k, G, m->cfg.ep_rank, home, counts, (float *const *)xc->dptr, (int32_t *const *)(xc->dptr + G));
+    QE_CHECK(cudaGetLastError());
+    xc->T = T;
+    g_launches += 2;
+    return 0;
+}
+
+int qe_moe_ep_experts_p2p(QeMoe *m, QeEpXchg *xc, int T, void *stream) {
+    if (!m || !xc || T < 1 || T > xc->Tmax) QE_FAIL("ep_experts_p2p: bad arguments");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int G = m->cfg.ep_size, n = G * T, P = std::min(n, m->cfg.max_tokens), k = m->cfg.top_k;
+    const size_t H = m->cfg.hidden;
+    if (ensure_ws(d, scratch_layout(m->cfg, P, nullptr, nullptr))) return -1;
+    Scratch sc;
+    scratch_layout(m->cfg, P, (char *)d->ws, &sc);
+    const float *rx = (const float *)xc->mine;
+    const int32_t *rm = (const int32_t *)(xc->mine + xc->off_meta);
+    for (int r0 = 0; r0 < n; r0 += P) {
+        const int cnt = std::min(P, n - r0);
+        ep_local_kernel<<<(cnt * k + 255) / 256, 256, 0, s>>>(rm + (size_t)r0 * 2 * k, cnt, k, m->e0, m->E_loc,
+                                                             sc.idx, sc.score);
+        QE_CHECK(cudaGetLastError());
+        const EpScatter sca = {(float *const *)(xc->dptr + 2 * G), r0, T, m->cfg.ep_rank};
+        if (run_experts(m, rx + (size_t)r0 * H, nullptr, cnt, sc, d->sms, true, false, s, &sca)) return -1;
+        g_launches += 1;
+    }
+    /* the partial rows written into the peers must be visible to them once this stream's work is done */
+    return 0;
+}
+
+int qe_moe_ep_combine_p2p(QeMoe *m, QeEpXchg *xc, int T, const int32_t *home, const float *shared, float *out,
+                          void *stream) {
+    if (!xc || T < 1 || T > xc->Tmax) QE_FAIL("ep_combine_p2p: bad arguments");
+    return qe_moe_ep_combine_device(m, T, (const float *)(xc->mine + xc->off_back), home, shared, out, stream);
 }
 
 int qe_qmat_matvec(const uint32_t *w, const uint16_t *scales, const uint16_t *biases, int rows, int cols, int bits,

@@ -10,7 +10,11 @@ e // (E / world); the router and the shared expert are replicated. Two step shap
   rank order plus the gated shared expert;
 * replicated (decode): every rank holds the same tokens, computes the partial sums of its own experts, and
   the partials are all-gathered and summed in rank order (deterministic, unlike a reduction whose order
-  depends on the collective's algorithm).
+  depends on the collective's algorithm);
+* p2p: the token-sharded step with the exchange done by the library's kernels through peer memory: the
+  packing kernel stores each row straight into its destination rank's receive buffer (NVLink, CUDA IPC
+  mappings), and the expert stage's combine stores each partial row straight into its home rank's return
+  buffer; NCCL only provides the two barriers (one-element all_reduce). Same arithmetic, bit-identical.
 
 The arithmetic runs in an engine: `DeviceEngine` calls libqengine_b200's qe_moe_ep_* entry points on the
 rank's GPU (the product path). Tests substitute a CPU engine with the same contract to check the exchange
@@ -61,6 +65,41 @@ class DeviceEngine:
                                           self._p(shared), self._p(out), self._s()):
             raise EngineError("qe_moe_ep_combine_device failed")
 
+    # ---- exchange through peer memory
+    xchg = None
+
+    def xchg_create(self, t_max: int) -> bytes:
+        nb = lib().qe_ep_xchg_handle_bytes()
+        handle = (C.c_uint8 * nb)()
+        self.xchg = lib().qe_ep_xchg_create(self.block.handle, t_max, handle)
+        if not self.xchg:
+            raise EngineError("qe_ep_xchg_create failed")
+        return bytes(handle)
+
+    def xchg_connect(self, handles: bytes) -> None:
+        buf = (C.c_uint8 * len(handles)).from_buffer_copy(handles)
+        if lib().qe_ep_xchg_connect(self.xchg, buf):
+            raise EngineError("qe_ep_xchg_connect failed")
+
+    def xchg_free(self) -> None:
+        if self.xchg:
+            lib().qe_ep_xchg_free(self.xchg)
+            self.xchg = None
+
+    def dispatch_p2p(self, x, meta, home, counts):
+        if lib().qe_moe_ep_dispatch_p2p(self.block.handle, self.xchg, x.shape[0], self._p(x), self._p(meta),
+                                        self._p(home), self._p(counts), self._s()):
+            raise EngineError("qe_moe_ep_dispatch_p2p failed")
+
+    def experts_p2p(self, T: int):
+        if lib().qe_moe_ep_experts_p2p(self.block.handle, self.xchg, T, self._s()):
+            raise EngineError("qe_moe_ep_experts_p2p failed")
+
+    def combine_p2p(self, T: int, home, shared, out):
+        if lib().qe_moe_ep_combine_p2p(self.block.handle, self.xchg, T, self._p(home), self._p(shared), self._p(out),
+                                       self._s()):
+            raise EngineError("qe_moe_ep_combine_p2p failed")
+
 
 class ExpertParallelMoe:
     """One routed MoE block, experts sharded over `group` (default: the world), one rank per GPU."""
@@ -82,11 +121,31 @@ class ExpertParallelMoe:
     def _empty(self, *shape, dtype=torch.float32):
         return torch.empty(*shape, dtype=dtype, device=self.device)
 
+    def enable_p2p(self, t_max: int) -> None:
+        """Create this rank's exchange buffers and map every other rank's (collective: all ranks call it)."""
+        h = self.engine.xchg_create(t_max)
+        mine = torch.tensor(list(h), dtype=torch.uint8, device=self.device)
+        allh = torch.empty(self.world * len(h), dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(allh, mine, group=self.group)
+        self.engine.xchg_connect(bytes(allh.cpu().numpy().tobytes()))
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.t_max = t_max
+        dist.barrier(group=self.group)
+
+    def _barrier(self) -> None:
+        dist.all_reduce(self._flag, group=self.group)   # stream-ordered: every rank's preceding kernels are done
+
+    def close(self) -> None:
+        if getattr(self.engine, "xchg", None):
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            self.engine.xchg_free()
+
     def forward(self, x: torch.Tensor, mode: str = "sharded", mark=None) -> torch.Tensor:
         """out[T][hidden] for this rank's x[T][hidden] (sharded), or for the tokens every rank holds
         (replicated). Every rank must call it with the same T and mode. mark(name), if given, is called
         after each phase (route, pack, dispatch, experts, return, combine), e.g. to record CUDA events."""
-        if mode not in ("sharded", "replicated"):
+        if mode not in ("sharded", "replicated", "p2p"):
             raise ValueError(f"mode {mode!r}")
         mark = mark or (lambda name: None)
         T, H, k, G = x.shape[0], self.hidden, self.top_k, self.world
@@ -104,6 +163,20 @@ class ExpertParallelMoe:
             mark("return")
             self.engine.combine(parts, None, shared, out)
             mark("combine")
+            return out
+        if mode == "p2p":
+            home, counts = self._empty(G, T, dtype=torch.int32), self._empty(G, dtype=torch.int32)
+            self.engine.dispatch_p2p(x, meta, home, counts)
+            mark("pack")
+            self._barrier()
+            mark("dispatch")
+            self.engine.experts_p2p(T)
+            mark("experts")
+            self._barrier()
+            mark("return")
+            self.engine.combine_p2p(T, home, shared, out)
+            mark("combine")
+            self.last_counts = counts
             return out
         send_x, send_meta = self._empty(G, T, H), self._empty(G, T, 2 * k, dtype=torch.int32)
         home, counts = self._empty(G, T, dtype=torch.int32), self._empty(G, dtype=torch.int32)

@@ -76,6 +76,15 @@ def lib() -> C.CDLL:
         L.qe_moe_ep_experts_device.argtypes = [vp, C.c_int, vp, vp, vp, vp]
         L.qe_moe_ep_combine_device.argtypes = [vp, C.c_int, vp, vp, vp, vp, vp]
         L.qe_moe_ep_size.argtypes = [vp]
+        L.qe_ep_xchg_create.restype = vp
+        L.qe_ep_xchg_create.argtypes = [vp, C.c_int, vp]
+        L.qe_ep_xchg_handle_bytes.restype = C.c_int
+        L.qe_ep_xchg_connect.argtypes = [vp, vp]
+        L.qe_ep_xchg_connect_local.argtypes = [vp, C.c_int]
+        L.qe_ep_xchg_free.argtypes = [vp]
+        L.qe_moe_ep_dispatch_p2p.argtypes = [vp, vp, C.c_int, vp, vp, vp, vp, vp]
+        L.qe_moe_ep_experts_p2p.argtypes = [vp, vp, C.c_int, vp]
+        L.qe_moe_ep_combine_p2p.argtypes = [vp, vp, C.c_int, vp, vp, vp, vp]
         L.qe_moe_open_safetensors.restype = vp
         L.qe_moe_open_safetensors.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(QeMoeConfig)]
         L.qe_safetensors_tensor_info.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(C.c_int64),

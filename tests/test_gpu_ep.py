@@ -57,6 +57,53 @@ def _emulated_sharded_step(blocks, xs):
     return outs, [m.cpu().numpy() for m in meta], [c.cpu().numpy() for c in counts]
 
 
+def _emulated_p2p_step(blocks, xs):
+    """The peer-memory step with G emulated ranks on one GPU (contexts connected with plain pointers)."""
+    import ctypes as C
+    from qmoe.ep import DeviceEngine
+    from qmoe.lib import lib
+    G, T, H = len(blocks), xs[0].shape[0], xs[0].shape[1]
+    k = blocks[0].top_k
+    dev = xs[0].device
+    eng = [DeviceEngine(b) for b in blocks]
+    for e in eng:
+        e.xchg_create(T)
+    arr = (C.c_void_p * G)(*[e.xchg for e in eng])
+    assert lib().qe_ep_xchg_connect_local(arr, G) == 0
+    meta = [torch.empty(T, 2 * k, dtype=torch.int32, device=dev) for _ in range(G)]
+    shared = [torch.empty(T, H, device=dev) for _ in range(G)]
+    home = [torch.empty(G, T, dtype=torch.int32, device=dev) for _ in range(G)]
+    counts = [torch.empty(G, dtype=torch.int32, device=dev) for _ in range(G)]
+    for r in range(G):
+        eng[r].route(xs[r], meta[r], shared[r])
+        eng[r].dispatch_p2p(xs[r], meta[r], home[r], counts[r])
+    for d in range(G):
+        eng[d].experts_p2p(T)
+    outs = []
+    for r in range(G):
+        out = torch.empty(T, H, device=dev)
+        eng[r].combine_p2p(T, home[r], shared[r], out)
+        outs.append(out)
+    torch.cuda.synchronize()
+    res = [o.cpu().numpy() for o in outs]
+    for e in eng:
+        e.xchg_free()
+    return res
+
+
+@pytest.mark.parametrize("G,T", [(1, 16), (2, 64), (4, 24), (8, 5)])
+def test_ep_p2p_emulated_equals_all_to_all(G, T):
+    blocks = _blocks(CFG, G)
+    gen = torch.Generator().manual_seed(500 + G + T)
+    xs = [torch.randn(T, CFG.hidden, generator=gen).cuda() for _ in range(G)]
+    want, _, _ = _emulated_sharded_step(blocks, xs)
+    got = _emulated_p2p_step(blocks, xs)
+    for r in range(G):
+        assert np.array_equal(got[r].view(np.uint32), want[r].cpu().numpy().view(np.uint32)), f"rank {r}"
+    for b in blocks:
+        b.close()
+
+
 def _rel(a, b):
     return np.linalg.norm(a - b, axis=1) / np.maximum(np.linalg.norm(b, axis=1), 1e-30)
 
@@ -129,22 +176,25 @@ def _nccl_worker(rank, world, port, mode, q):
     try:
         from qmoe.ep import ExpertParallelMoe
         ep = ExpertParallelMoe.on_gpu(CFG, rank, world, rank, seed=5)
+        if mode == "p2p":
+            ep.enable_p2p(64)
         ref = qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, device=rank)
         T = 48
-        gen = torch.Generator().manual_seed(1000 + (rank if mode == "sharded" else 0))
+        gen = torch.Generator().manual_seed(1000 + (rank if mode != "replicated" else 0))
         x = torch.randn(T, CFG.hidden, generator=gen).cuda(rank)
         out = ep.forward(x, mode=mode)
         want = torch.empty_like(x)
         ref.forward_device(T, x.data_ptr(), want.data_ptr(), torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
         q.put((rank, float(_rel(out.cpu().numpy(), want.cpu().numpy()).max())))
+        ep.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["sharded", "replicated"])
+@pytest.mark.parametrize("mode", ["sharded", "replicated", "p2p"])
 def test_ep_nccl_two_gpus(mode):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")

@@ -499,8 +499,41 @@ int qe_launch_down(const QeExpertArgs *a, const float *h3, int ldh, const QeBuck
     return dispatch<MODE_DOWN>(a, h3, ldh, b, T, ybuf, a->hidden, grid, s);
 }
 
+/* Same as combine_kernel, 4 consecutive outputs per thread with 16-byte loads and stores (H % 4 == 0). */
+__global__ void combine4_kernel(const float *__restrict__ ybuf, const float *__restrict__ score,
+                                const float *__restrict__ logits, int ld_logits, int T, int E, int k, int H,
+                                float *__restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;   /* float4 index */
+    const int H4 = H / 4;
+    if (i >= (long long)T * H4) return;
+    const int t = (int)(i / H4), j4 = (int)(i % H4);
+    const float4 *y = reinterpret_cast<const float4 *>(ybuf + (size_t)t * (k + 1) * H) + j4;
+    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int s = 0; s < k; s++) {
+        const float sc = score[(size_t)t * k + s];
+        const float4 v = y[(size_t)s * H4];
+        o.x = __fadd_rn(o.x, __fmul_rn(sc, v.x));
+        o.y = __fadd_rn(o.y, __fmul_rn(sc, v.y));
+        o.z = __fadd_rn(o.z, __fmul_rn(sc, v.z));
+        o.w = __fadd_rn(o.w, __fmul_rn(sc, v.w));
+    }
+    const float sg = qe_sigmoid(logits[(size_t)t * ld_logits + E]);
+    const float4 v = y[(size_t)k * H4];
+    o.x = __fadd_rn(o.x, __fmul_rn(sg, v.x));
+    o.y = __fadd_rn(o.y, __fmul_rn(sg, v.y));
+    o.z = __fadd_rn(o.z, __fmul_rn(sg, v.z));
+    o.w = __fadd_rn(o.w, __fmul_rn(sg, v.w));
+    reinterpret_cast<float4 *>(out)[i] = o;
+}
+
 int qe_launch_combine(const float *ybuf, const float *score, const float *logits, int ld_logits, int T, int E, int k,
                       int H, float *out, cudaStream_t s) {
+    if (H % 4 == 0 && ((uintptr_t)ybuf | (uintptr_t)out) % 16 == 0) {
+        const long long n4 = (long long)T * (H / 4);
+        combine4_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(ybuf, score, logits, ld_logits, T, E, k, H, out);
+        QE_CHECK(cudaGetLastError());
+        return 0;
+    }
     const long long n = (long long)T * H;
     combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ybuf, score, logits, ld_logits, T, E, k, H, out);
     QE_CHECK(cudaGetLastError());

@@ -60,6 +60,15 @@ int qe_launch_combine_sel_scatter(const float *ybuf, const int32_t *idx, const f
                                   float *const *dst_base /* device [G] */, int row0, int Tblk, int self,
                                   cudaStream_t s);
 
+/* Decode GEMVs (decode.cu): gate/up + SwiGLU per (token, slot) pair into h3 [T*(k+1)][ldh], then down + the
+ * weighted combine (top-k order, then the gated shared expert) into out [T][hidden]. */
+bool qe_decode_supported(const QeExpertArgs *a);
+int qe_launch_decode_gateup(const QeExpertArgs *a, const float *x, const int32_t *idx, int T, float *h3, int ldh,
+                            cudaStream_t s);
+int qe_launch_decode_down_combine(const QeExpertArgs *a, const float *h3, int ldh, const int32_t *idx,
+                                  const float *score, const float *logits, int ld_logits, int T, float *out,
+                                  cudaStream_t s);
+
 /* Generic quantized matrix-vector products (engine/src/qmat.c:15-49 semantics) over T vectors. */
 int qe_launch_qmatvec(const QeQDev *m, const float *x, int T, float *y, cudaStream_t s);
 

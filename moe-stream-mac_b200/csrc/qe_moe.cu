@@ -25,8 +25,10 @@
 
 int qe_expert_rows_per_cta(int T);
 
-/* Batches of at least this many tokens take the tensor-core (tcgen05) expert path when the shape allows. */
+/* Batches of at least this many tokens take the tensor-core (tcgen05) expert path when the shape allows;
+ * batches of at most kDecodeMaxTokens take the decode GEMVs (decode.cu); the mma.sync kernels take the rest. */
 static constexpr int kTcMinTokens = 64;
+static constexpr int kDecodeMaxTokens = 4;
 
 /* ------------------------------------------------------------------ per-device context and workspace */
 
@@ -169,6 +171,7 @@ struct QeMoe {
     int e0, E_loc;          /* routed experts held here: global ids [e0, e0 + E_loc) (expert parallelism) */
     int path;               /* 0 = auto, 1 = mma.sync only, 2 = tensor-core (tcgen05) whenever supported */
     bool tc;                /* tensor-core path available for this shape */
+    bool decode;            /* decode GEMVs available for this shape */
     alignas(64) unsigned char maps_gu[2 * 2 * 3 * 128];  /* [routed/shared][gate/up][codes, scales, biases] */
     alignas(64) unsigned char maps_dn[2 * 3 * 128];      /* [routed/shared][codes, scales, biases] */
 };
@@ -258,9 +261,10 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     m->ex.E = El; m->ex.k = c->top_k; m->ex.hidden = H; m->ex.inter = I; m->ex.sh_inter = Is;
     size_t wb, gb;
     m->expert_bytes = qbytes(1, I, H, b, gs, &wb, &gb) * 2 + qbytes(1, H, I, b, gs, &wb, &gb);
-    const char *path = getenv("QE_EXPERT_PATH");   /* auto (default) | mma | tc */
-    m->path = path && !strcmp(path, "mma") ? 1 : path && !strcmp(path, "tc") ? 2 : 0;
+    const char *path = getenv("QE_EXPERT_PATH");   /* auto (default) | mma | tc | gemv */
+    m->path = path && !strcmp(path, "mma") ? 1 : path && !strcmp(path, "tc") ? 2 : path && !strcmp(path, "gemv") ? 3 : 0;
     m->tc = qe_tc_supported(&m->ex);
+    m->decode = qe_decode_supported(&m->ex);
     if (m->tc) {
         const size_t mb = qe_tc_map_bytes();
         const QeQDev *gu[2][2] = {{&m->ex.gate, &m->ex.up}, {&m->ex.sh_gate, &m->ex.sh_up}};
@@ -501,6 +505,18 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     g_launches += 1;
     prof_mark(dev, s);
     const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
+    if (m->decode && (m->path == 3 || (m->path == 0 && T <= kDecodeMaxTokens))) {
+        /* decode: CUDA-core GEMVs over each selected expert's codes, combine fused into the down projection */
+        prof_mark(dev, s);   /* no bucketing */
+        if (qe_launch_decode_gateup(&m->ex, x, sc.idx, T, sc.h3, I, s)) return -1;
+        prof_mark(dev, s);
+        if (qe_launch_decode_down_combine(&m->ex, sc.h3, I, sc.idx, sc.score, sc.logits, c.E + 1, T, out, s))
+            return -1;
+        prof_mark(dev, s);
+        prof_mark(dev, s);   /* combine: fused into down */
+        g_launches += 2;
+        return 0;
+    }
     const bool use_tc = m->tc && (m->path == 2 || (m->path == 0 && T >= kTcMinTokens));
     if (use_tc) {
         const int R = qe_tc_bm(), NB = qe_tc_bn();

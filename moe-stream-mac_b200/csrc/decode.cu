@@ -25,43 +25,71 @@ namespace {
 constexpr int kThreads = 256;   /* 8 warps */
 constexpr int kGS = 64;
 
-/* code -> exact float via the 2^23 magic number */
-__device__ __forceinline__ float code_f(uint32_t q) { return __uint_as_float(0x4B000000u | q) - 8388608.0f; }
+/* Code q as the float 1 + q/16 (4-bit) or 1 + q/256 (8-bit): the code's bits are the top mantissa bits, one
+ * shift and one logic op. Sum_i (1 + q_i/2^b) x_i - Sum_i x_i = 2^-b Sum_i q_i x_i, so a lane forms its dot
+ * with paired fp32 FMAs and subtracts its chunk's x sum; the cancellation costs ~2 bits of the 24 (the terms
+ * are within a factor ~2 of the result). */
+template <int BITS, int I>
+__device__ __forceinline__ float code_v(uint32_t w) {
+    constexpr int kTop = 23 - BITS;                 /* mantissa position of the code's lowest bit */
+    constexpr int kSh = kTop - BITS * I;            /* left shift bringing code I there */
+    constexpr uint32_t kMask = ((1u << BITS) - 1u) << kTop;
+    const uint32_t s = kSh >= 0 ? (w << (kSh >= 0 ? kSh : 0)) : (w >> (kSh < 0 ? -kSh : 0));
+    return __uint_as_float((s & kMask) | 0x3F800000u);
+}
 
-/* dot of one lane's 16 code bytes with its x values (sequential fp32) */
+/* 2^-b * (dot of one lane's 16 code bytes with its x values), given the lane's x sum */
 template <int BITS>
-__device__ __forceinline__ float lane_dot(const uint4 w, const float *xs) {
+__device__ __forceinline__ float lane_dot(const uint4 w, const float *xs, float xsum) {
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-    float a = 0.0f;
+    float2 a = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int q = 0; q < 4; q++) {
         if constexpr (BITS == 4) {
-#pragma unroll
-            for (int i = 0; i < 8; i++) a = __fmaf_rn(code_f((ws[q] >> (4 * i)) & 15u), xs[q * 8 + i], a);
+            a = __ffma2_rn(make_float2(code_v<4, 0>(ws[q]), code_v<4, 1>(ws[q])), make_float2(xs[q * 8], xs[q * 8 + 1]), a);
+            a = __ffma2_rn(make_float2(code_v<4, 2>(ws[q]), code_v<4, 3>(ws[q])), make_float2(xs[q * 8 + 2], xs[q * 8 + 3]), a);
+            a = __ffma2_rn(make_float2(code_v<4, 4>(ws[q]), code_v<4, 5>(ws[q])), make_float2(xs[q * 8 + 4], xs[q * 8 + 5]), a);
+            a = __ffma2_rn(make_float2(code_v<4, 6>(ws[q]), code_v<4, 7>(ws[q])), make_float2(xs[q * 8 + 6], xs[q * 8 + 7]), a);
         } else {
-#pragma unroll
-            for (int i = 0; i < 4; i++) a = __fmaf_rn(code_f((ws[q] >> (8 * i)) & 255u), xs[q * 4 + i], a);
+            a = __ffma2_rn(make_float2(code_v<8, 0>(ws[q]), code_v<8, 1>(ws[q])), make_float2(xs[q * 4], xs[q * 4 + 1]), a);
+            a = __ffma2_rn(make_float2(code_v<8, 2>(ws[q]), code_v<8, 3>(ws[q])), make_float2(xs[q * 4 + 2], xs[q * 4 + 3]), a);
         }
     }
-    return a;
+    return __fsub_rn(__fadd_rn(a.x, a.y), xsum);
 }
 
-/* R row-vectors (pointers to their first code byte, bytes per row = NL*SW*16), row r dotted with x[r]
- * (shared memory, fp32) by a sub-warp of SW lanes; sc/bi: scale/bias of (row, group g) at sc[g * gstride];
- * gsum[r]: group sums of x[r]. Returns the row totals in every lane of the sub-warp. */
+/* Shared-memory vectors are stored with their 16-byte pieces swizzled within each lane chunk (Q pieces):
+ * piece q of chunk c sits at q ^ (c % Q), so the 32 lanes of a warp, reading piece q of consecutive chunks,
+ * hit distinct banks. */
+template <int Q>
+__device__ __forceinline__ int swz(int c, int q) { return q ^ (c & (Q - 1)); }
+
+/* The code words of R rows (bytes per row = NL*SW*16) for one sub-warp lane, and the scale and bias of each
+ * lane-load's group (bf16 pairs, scale in the low half), all requested together. */
 template <int BITS, int SW, int NL, int R>
-__device__ __forceinline__ void subwarp_rows(const uint8_t *const (&rows)[R], const uint16_t *const (&sc)[R],
-                                             const uint16_t *const (&bi)[R], size_t gstride,
-                                             const float *const (&x)[R], const float *const (&gsum)[R], int sl,
-                                             float (&tot)[R]) {
-    constexpr int CPL = 128 / BITS;   /* codes per lane-load */
-    constexpr int LPG = kGS / CPL;    /* lanes per group */
-    uint4 w[R][NL];
+__device__ __forceinline__ void load_rows(const uint8_t *const (&rows)[R], const uint16_t *const (&sc)[R],
+                                          const uint16_t *const (&bi)[R], size_t gstride, int sl, uint4 (&w)[R][NL],
+                                          uint32_t (&sb)[R][NL]) {
+    constexpr int LPG = kGS / (128 / BITS);
 #pragma unroll
     for (int r = 0; r < R; r++)
 #pragma unroll
-        for (int i = 0; i < NL; i++)
+        for (int i = 0; i < NL; i++) {
             w[r][i] = __ldg(reinterpret_cast<const uint4 *>(rows[r]) + i * SW + sl);
+            const size_t g = (size_t)((i * SW + sl) / LPG) * gstride;
+            sb[r][i] = (uint32_t)__ldg(sc[r] + g) | ((uint32_t)__ldg(bi[r] + g) << 16);
+        }
+}
+
+/* Row r's loaded codes dotted with x[r] (shared memory, fp32) by a sub-warp of SW lanes; cs[r]: x[r]'s sums
+ * per lane chunk (128/BITS elements), gsum[r]: per group of 64; sc/bi: scale/bias of (row, group g) at
+ * sc[g * gstride]. Returns the row totals in every lane of the sub-warp. */
+template <int BITS, int SW, int NL, int R, bool SAMEX>
+__device__ __forceinline__ void dot_rows(const uint4 (&w)[R][NL], const uint32_t (&sb)[R][NL],
+                                         const float *const (&x)[R], const float *const (&cs)[R],
+                                         const float *const (&gsum)[R], int sl, float (&tot)[R]) {
+    constexpr int CPL = 128 / BITS;   /* codes per lane-load */
+    constexpr int LPG = kGS / CPL;    /* lanes per group */
     float acc[R];
 #pragma unroll
     for (int r = 0; r < R; r++) acc[r] = 0.0f;
@@ -69,24 +97,24 @@ __device__ __forceinline__ void subwarp_rows(const uint8_t *const (&rows)[R], co
     for (int i = 0; i < NL; i++) {
         const int lp = i * SW + sl;          /* lane-load position in the row */
         const int g = lp / LPG;
+        float xs[CPL];
 #pragma unroll
         for (int r = 0; r < R; r++) {
-            /* rows sharing one x vector (gate/up) re-read it from shared memory: broadcast, cheap */
-            float xs[CPL];
-            const float4 *x4 = reinterpret_cast<const float4 *>(x[r] + lp * CPL);
+            if (r == 0 || !SAMEX) {   /* rows sharing one vector (gate/up) read it once */
+                const float4 *x4 = reinterpret_cast<const float4 *>(x[r]) + lp * (CPL / 4);
 #pragma unroll
-            for (int q = 0; q < CPL / 4; q++) {
-                const float4 v = x4[q];
-                xs[4 * q] = v.x; xs[4 * q + 1] = v.y; xs[4 * q + 2] = v.z; xs[4 * q + 3] = v.w;
+                for (int q = 0; q < CPL / 4; q++) {
+                    const float4 v = x4[swz<CPL / 4>(lp, q)];
+                    xs[4 * q] = v.x; xs[4 * q + 1] = v.y; xs[4 * q + 2] = v.z; xs[4 * q + 3] = v.w;
+                }
             }
-            const float gs = gsum[r][g];
-            float part = lane_dot<BITS>(w[r][i], xs);
+            float part = lane_dot<BITS>(w[r][i], xs, cs[r][lp]);
 #pragma unroll
             for (int o = 1; o < LPG; o <<= 1) part = __fadd_rn(part, __shfl_xor_sync(QE_FULL, part, o));
             if (lp % LPG == 0) {
-                const float s = qe_bf16_to_f32(__ldg(sc[r] + (size_t)g * gstride));
-                const float b = qe_bf16_to_f32(__ldg(bi[r] + (size_t)g * gstride));
-                acc[r] = __fadd_rn(acc[r], __fmaf_rn(s, part, __fmul_rn(b, gs)));
+                const float sq = __fmul_rn(part, (float)(1 << BITS));   /* exact: a power of two */
+                const float s = __uint_as_float(sb[r][i] << 16), b = __uint_as_float(sb[r][i] & 0xFFFF0000u);
+                acc[r] = __fadd_rn(acc[r], __fmaf_rn(s, sq, __fmul_rn(b, gsum[r][g])));
             }
         }
     }
@@ -99,14 +127,33 @@ __device__ __forceinline__ void subwarp_rows(const uint8_t *const (&rows)[R], co
     }
 }
 
-/* x [K] into shared memory with its per-group sums (sequential within a group, like qmat.c:27-32). */
-__device__ void stage_vec(const float *__restrict__ src, int K, float *xs, float *gsum) {
-    for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = src[i];
+/* n vectors of K floats into shared memory (vs[j*ldv + c]) with their sums per chunk of `chunk` elements
+ * (cs[j*(ldv/chunk) + c]) and per group of 64 (gs[j*(ldv/64) + g]), all sequential in element order.
+ * src(j) gives vector j's global address. */
+template <int CHUNK, typename Src>
+__device__ void stage_vecs(Src src, int n, int K, int ldv, float *vs, float *cs, float *gs) {
+    constexpr int Q = CHUNK / 4;
+    for (int i = threadIdx.x; i < n * ldv; i += blockDim.x) {
+        const int j = i / ldv, c = i % ldv;
+        const int ch = c / CHUNK, q = (c % CHUNK) / 4;
+        vs[(size_t)j * ldv + ch * CHUNK + swz<Q>(ch, q) * 4 + (c & 3)] = c < K ? src(j)[c] : 0.0f;
+    }
     __syncthreads();
-    for (int g = threadIdx.x; g < K / kGS; g += blockDim.x) {
+    const int nc = ldv / CHUNK;
+    for (int i = threadIdx.x; i < n * nc; i += blockDim.x) {
+        const int ch = i % nc;
+        const float *v = vs + (size_t)(i / nc) * ldv + (size_t)ch * CHUNK;
         float s = 0.0f;
-        for (int i = 0; i < kGS; i++) s = __fadd_rn(s, xs[g * kGS + i]);
-        gsum[g] = s;
+        for (int c = 0; c < CHUNK; c++) s = __fadd_rn(s, v[swz<Q>(ch, c / 4) * 4 + (c & 3)]);
+        cs[i] = s;
+    }
+    __syncthreads();
+    const int ng = ldv / kGS, per = kGS / CHUNK;
+    for (int i = threadIdx.x; i < n * ng; i += blockDim.x) {
+        const float *c = cs + (size_t)(i / ng) * nc + (size_t)(i % ng) * per;
+        float s = 0.0f;
+        for (int q = 0; q < per; q++) s = __fadd_rn(s, c[q]);
+        gs[i] = s;
     }
     __syncthreads();
 }
@@ -151,8 +198,8 @@ __global__ void __launch_bounds__(kThreads) decode_gateup_kernel(QeExpertArgs a,
     const int e = shared ? 0 : idx[(size_t)t * k + j];
     const QeQDev &G = shared ? a.sh_gate : a.gate, &U = shared ? a.sh_up : a.up;
     const int rows = G.rows, K = G.cols;
-    float *xs = smem, *gsum = smem + K;
-    stage_vec(x + (size_t)t * K, K, xs, gsum);
+    constexpr int CPL = 128 / BITS;
+    float *xs = smem, *cs = smem + K, *gsum = cs + K / CPL;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int SUBS = 32 / SW;
     const int sub = lane / SW, sl = lane % SW;
@@ -160,28 +207,39 @@ __global__ void __launch_bounds__(kThreads) decode_gateup_kernel(QeExpertArgs a,
     const int r1 = min(rows, r0 + rows_per_cta);
     /* sub-warp (warp, sub) owns rows rb .. rb+kR-1 of each pass; the loop bound is the warp's first row so
      * every lane of a warp runs the same iterations (the shuffles need all 32); past r1, rows are clamped and
-     * their results dropped */
-    for (int rw = r0 + warp * SUBS * kR; rw < r1; rw += (kThreads / 32) * SUBS * kR) {
+     * their results dropped. The first pass's code words are requested before x is staged. */
+    bool staged = false;
+    for (int rw = r0 + warp * SUBS * kR; ; rw += (kThreads / 32) * SUBS * kR) {
+        const bool work = rw < r1;
         const int rb = rw + sub * kR;
         const uint8_t *rp[2 * kR];
         const uint16_t *sp[2 * kR], *bp[2 * kR];
         size_t gstride = 0;
 #pragma unroll
         for (int q = 0; q < kR; q++) {
-            const int row = min(rb + q, r1 - 1);
+            const int row = max(r0, min(rb + q, r1 - 1));
             const QRow g = qrow(G, e, row), u = qrow(U, e, row);
             rp[2 * q] = g.codes; sp[2 * q] = g.sc; bp[2 * q] = g.bi;
             rp[2 * q + 1] = u.codes; sp[2 * q + 1] = u.sc; bp[2 * q + 1] = u.bi;
             gstride = g.gstride;
         }
+        uint4 w[2 * kR][NL];
+        uint32_t sb[2 * kR][NL];
+        if (work) load_rows<BITS, SW, NL, 2 * kR>(rp, sp, bp, gstride, sl, w, sb);
+        if (!staged) {   /* every thread reaches this once, on its first iteration */
+            stage_vecs<CPL>([&](int) { return x + (size_t)t * K; }, 1, K, K, xs, cs, gsum);
+            staged = true;
+        }
+        if (!work) break;
         float tot[2 * kR];
-        const float *xr[2 * kR], *gr[2 * kR];
+        const float *xr[2 * kR], *cr[2 * kR], *gr[2 * kR];
 #pragma unroll
         for (int q = 0; q < 2 * kR; q++) {
             xr[q] = xs;
+            cr[q] = cs;
             gr[q] = gsum;
         }
-        subwarp_rows<BITS, SW, NL, 2 * kR>(rp, sp, bp, gstride, xr, gr, sl, tot);
+        dot_rows<BITS, SW, NL, 2 * kR, true>(w, sb, xr, cr, gr, sl, tot);
         if (sl == 0)
 #pragma unroll
             for (int q = 0; q < kR; q++)
@@ -197,41 +255,34 @@ __global__ void __launch_bounds__(kThreads) decode_down_combine_kernel(QeExpertA
                                                                        int E, int k, float *__restrict__ out,
                                                                        int rows_per_cta) {
     extern __shared__ __align__(16) float smem[];
+    constexpr int CPL = 128 / BITS;
     const int t = blockIdx.x;
     const int kp1 = k + 1;
-    const int Kr = a.down.cols, Ks = a.sh_down.cols, H = a.hidden;
-    const int Kmax = Kr > Ks ? Kr : Ks;
-    /* the token's k+1 activation vectors and their group sums */
-    float *hs = smem, *gsum = smem + (size_t)kp1 * Kmax;
-    for (int i = threadIdx.x; i < kp1 * Kmax; i += blockDim.x) {
-        const int j = i / Kmax, c = i % Kmax;
-        const int Kj = j == k ? Ks : Kr;
-        hs[i] = c < Kj ? h3[((size_t)t * kp1 + j) * ldh + c] : 0.0f;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < kp1 * (Kmax / kGS); i += blockDim.x) {
-        const int j = i / (Kmax / kGS), g = i % (Kmax / kGS);
-        float s = 0.0f;
-        for (int c = 0; c < kGS; c++) s = __fadd_rn(s, hs[(size_t)j * Kmax + g * kGS + c]);
-        gsum[i] = s;
-    }
-    __syncthreads();
+    const int K = a.down.cols, H = a.hidden;   /* the shared expert's down has the same K (checked at launch) */
+    /* the token's k+1 activation vectors, their chunk sums and group sums */
+    float *hs = smem, *cs = hs + (size_t)kp1 * K, *gsum = cs + (size_t)kp1 * (K / CPL);
     const float sg = qe_sigmoid(logits[(size_t)t * ld_logits + E]);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int SUBS = 32 / SW;
     const int sub = lane / SW, sl = lane % SW;
     const int r0 = blockIdx.y * rows_per_cta, r1 = min(H, r0 + rows_per_cta);
     /* a sub-warp takes one output row at a time and its k+1 slots (routed experts, then the shared one) in
-     * passes of kRD, all loads of a pass in flight together; the combine runs in slot order (moe_layer.c:79-88) */
-    constexpr int kRD = 3;
-    for (int rw = r0 + warp * SUBS; rw < r1; rw += (kThreads / 32) * SUBS) {
+     * passes of kRD, all loads of a pass in flight together; the combine runs in slot order (moe_layer.c:79-88).
+     * The loop bound is warp-uniform (shuffles need all lanes); clamped rows are dropped. The first pass's code
+     * words are requested before the activations are staged. */
+    /* slots per pass: all 9 of a top-8 block when a row is one load per lane, fewer for longer rows (about 10
+     * loads in flight per lane) */
+    constexpr int kRD = NL <= 1 ? 9 : NL == 2 ? 5 : NL <= 4 ? 3 : 1;
+    bool staged = false;
+    for (int rw = r0 + warp * SUBS; ; rw += (kThreads / 32) * SUBS) {
+        const bool work = rw < r1;
         const bool live = rw + sub < r1;
-        const int row = live ? rw + sub : r1 - 1;   /* warp-uniform trip count; clamped rows are dropped */
+        const int row = live ? rw + sub : r1 - 1;
         float y[17];
         for (int j0 = 0; j0 < kp1; j0 += kRD) {
             const uint8_t *rp[kRD];
             const uint16_t *sp[kRD], *bp[kRD];
-            const float *xr[kRD], *gr[kRD];
+            const float *xr[kRD], *cr[kRD], *gr[kRD];
             size_t gstride = 0;
 #pragma unroll
             for (int q = 0; q < kRD; q++) {
@@ -239,15 +290,25 @@ __global__ void __launch_bounds__(kThreads) decode_down_combine_kernel(QeExpertA
                 const QRow d = j == k ? qrow(a.sh_down, 0, row) : qrow(a.down, idx[(size_t)t * k + j], row);
                 rp[q] = d.codes; sp[q] = d.sc; bp[q] = d.bi;
                 gstride = d.gstride;   /* the same for routed and shared down (equal shapes) */
-                xr[q] = hs + (size_t)j * Kmax;
-                gr[q] = gsum + (size_t)j * (Kmax / kGS);
+                xr[q] = hs + (size_t)j * K;
+                cr[q] = cs + (size_t)j * (K / CPL);
+                gr[q] = gsum + (size_t)j * (K / kGS);
             }
+            uint4 w[kRD][NL];
+            uint32_t sb[kRD][NL];
+            if (work) load_rows<BITS, SW, NL, kRD>(rp, sp, bp, gstride, sl, w, sb);
+            if (!staged) {   /* every thread reaches this once, in its first pass */
+                stage_vecs<CPL>([&](int j) { return h3 + ((size_t)t * kp1 + j) * ldh; }, kp1, K, K, hs, cs, gsum);
+                staged = true;
+            }
+            if (!work) break;
             float tot[kRD];
-            subwarp_rows<BITS, SW, NL, kRD>(rp, sp, bp, gstride, xr, gr, sl, tot);
+            dot_rows<BITS, SW, NL, kRD, false>(w, sb, xr, cr, gr, sl, tot);
 #pragma unroll
             for (int q = 0; q < kRD; q++)
                 if (j0 + q < kp1) y[j0 + q] = tot[q];
         }
+        if (!work) break;
         if (sl == 0 && live) {
             float o = 0.0f;
             for (int j = 0; j < k; j++) o = __fadd_rn(o, __fmul_rn(score[(size_t)t * k + j], y[j]));
@@ -279,7 +340,7 @@ int launch_gateup_t(const QeExpertArgs *a, const float *x, const int32_t *idx, i
     const int rows = a->inter, K = a->hidden;
     const int rpc = 16;
     dim3 grid(T * (a->k + 1), (rows + rpc - 1) / rpc);
-    const size_t smem = sizeof(float) * ((size_t)K + K / kGS);
+    const size_t smem = sizeof(float) * ((size_t)K + K / (128 / BITS) + K / kGS);
     decode_gateup_kernel<BITS, SW, NL><<<grid, kThreads, smem, s>>>(*a, x, idx, a->k, h3, ldh, rpc);
     QE_CHECK(cudaGetLastError());
     return 0;
@@ -289,9 +350,10 @@ template <int BITS, int SW, int NL>
 int launch_down_t(const QeExpertArgs *a, const float *h3, int ldh, const int32_t *idx, const float *score,
                   const float *logits, int ld_logits, int T, float *out, cudaStream_t s) {
     const int rpc = 16;
-    const int Kmax = a->inter > a->sh_inter ? a->inter : a->sh_inter;
+    const int K = a->inter;
+    if (a->sh_inter != K) QE_FAIL("decode down: shared expert width %d != %d", a->sh_inter, K);
     dim3 grid(T, (a->hidden + rpc - 1) / rpc);
-    const size_t smem = sizeof(float) * ((size_t)(a->k + 1) * Kmax + (size_t)(a->k + 1) * (Kmax / kGS));
+    const size_t smem = sizeof(float) * (size_t)(a->k + 1) * ((size_t)K + K / (128 / BITS) + K / kGS);
     if (smem > 200 * 1024) QE_FAIL("decode down: %zu B of shared memory", smem);
     auto kern = decode_down_combine_kernel<BITS, SW, NL>;
     QE_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

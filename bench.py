@@ -183,10 +183,15 @@ def profiled_traffic(kernel: str, config: str):
 def expert_kernel_name(cfg, stage: str, T: int) -> str:
     """The kernel the library runs for this stage (tensor-core path for batches of 64 tokens or more when
     the shape allows it: group size 64, every matrix a whole number of 128-row tiles)."""
+    path = os.environ.get("QE_EXPERT_PATH", "auto")
     tc = (T >= 64 and cfg.group_size == 64 and all(d % 128 == 0 for d in (cfg.hidden, cfg.inter, cfg.sh_inter))
-          and os.environ.get("QE_EXPERT_PATH", "auto") != "mma")
+          and path != "mma")
+    decode = (T <= 4 and cfg.group_size == 64 and cfg.inter == cfg.sh_inter and path == "auto"
+              and (cfg.hidden * cfg.bits // 8) % 1024 == 0 and (cfg.inter * cfg.bits // 8) % 128 == 0)
     if tc:
         return f"tc_expert_kernel<{cfg.bits},{2 if stage == 'gateup' else 1}>"
+    if decode:
+        return f"decode_gateup_kernel<{cfg.bits}>" if stage == "gateup" else f"decode_down_combine_kernel<{cfg.bits}>"
     return f"expert_kernel<{cfg.bits},{cfg.group_size},{stage}>"
 
 
@@ -261,6 +266,8 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=16)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
+                    help="1 GPU: replay each block's forward as a captured CUDA graph (auto: decode batches, T <= 4)")
     ap.add_argument("--ep-mode", default="p2p", choices=["p2p", "sharded"],
                     help="N > 1: exchange through peer memory (p2p) or NCCL all_to_all (sharded)")
     args = ap.parse_args()
@@ -286,6 +293,7 @@ def main():
     out = torch.empty_like(x)
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
+    use_graph = False
     if ep:
         from qmoe.ep import ExpertParallelMoe
         models = [ExpertParallelMoe.on_gpu(cfg, rank, world, local, seed=b + 1, block=b, max_tokens=world * T)
@@ -303,6 +311,14 @@ def main():
 
         def step(i):
             blocks[i % len(blocks)].forward_device(T, x.data_ptr(), out.data_ptr(), sptr)
+
+        use_graph = args.graph == "on" or (args.graph == "auto" and T <= 4)
+        if use_graph:   # one captured forward per block, replayed (no per-kernel host launch cost)
+            graphs = [b.graph(T, x.data_ptr(), out.data_ptr()) for b in blocks]
+            eager_step = step
+
+            def step(i):
+                graphs[i % len(graphs)].launch(sptr)
 
     def barrier():
         if world > 1:
@@ -328,6 +344,12 @@ def main():
     launches = qmoe.kernel_launches() - launches0
     stage_ms, passes = qmoe.profile_end(local)
     clk = clocks.stop()
+    if not ep and use_graph:   # graphs carry no stage events: profile the same forwards eagerly, untimed
+        qmoe.profile_begin(local)
+        for i in range(min(args.steps, 50)):
+            eager_step(i)
+        torch.cuda.synchronize()
+        stage_ms, passes = qmoe.profile_end(local)
     ms = e0.elapsed_time(e1)
     t = torch.tensor([ms], device="cuda")
     if world > 1:
@@ -389,8 +411,9 @@ def main():
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(cfg, world, args.blocks, "rows and partial sums stored into peer memory by the "
-                                      "kernels" if args.ep_mode == "p2p" else "all_to_all over NCCL"),
+            "config": dict(workload_config(cfg, world, args.blocks, "rows and partial sums stored into peer memory by "
+                                           "the kernels" if args.ep_mode == "p2p" else "all_to_all over NCCL"),
+                           cuda_graph=use_graph),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * cfg.hidden,
                     "d2h_bytes_per_step": 4 * T * cfg.hidden, "steps": ke, "timing": "host clock, max over ranks"},
             "roofline": roofline, "gpu_launches": launches, "clocks": clk}
@@ -400,6 +423,9 @@ def main():
     if ep:
         for mdl in models:
             mdl.close()
+    if use_graph:
+        for g in graphs:
+            g.close()
     for b in blocks:
         b.close()
     if world > 1:

@@ -95,6 +95,15 @@ int qe_moe_forward(QeMoe *m, int T, const float *x, float *out);
  * no host synchronisation. */
 int qe_moe_forward_device(QeMoe *m, int T, const float *x, float *out, void *stream);
 
+/* qe_moe_forward_device of T tokens on fixed device buffers x/out, captured once into a CUDA graph and replayed
+ * by qe_moe_graph_launch on any stream of the handle's device (decode loops: the same T every step, no host
+ * launch overhead per kernel). The graph has its own scratch; the handle must outlive it, and replays of one
+ * graph must not overlap. No reference counterpart. NULL / -1 on failure. */
+typedef struct QeMoeGraph QeMoeGraph;
+QeMoeGraph *qe_moe_graph_create(QeMoe *m, int T, const float *x, float *out);
+int qe_moe_graph_launch(QeMoeGraph *g, void *stream);
+void qe_moe_graph_free(QeMoeGraph *g);
+
 /* Routing only (moe_layer.c:29-37): idx[T][top_k] expert ids, score[T][top_k] renormalised weights,
  * host buffers. */
 int qe_moe_route(QeMoe *m, int T, const float *x, int32_t *idx, float *score);

@@ -264,13 +264,11 @@ int qe_launch_decode_down_combine(const QeExpertArgs *a, const float *h3, int ld
     const size_t smem = sizeof(float) * (size_t)kp1 * ((size_t)K + K / kGS);
     if (smem > 200 * 1024) QE_FAIL("decode down: %zu B of shared memory", smem);
     if (a->gate.bits == 4) {
-        QE_CHECK(cudaFuncSetAttribute(decode_down_combine_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem));
+        QE_CHECK(qe_set_smem((const void *)decode_down_combine_kernel<4>, smem));
         decode_down_combine_kernel<4><<<grid, kp1 * 32, smem, s>>>(*a, h3, ldh, idx, score, logits, ld_logits, a->E,
                                                                    a->k, out);
     } else {
-        QE_CHECK(cudaFuncSetAttribute(decode_down_combine_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem));
+        QE_CHECK(qe_set_smem((const void *)decode_down_combine_kernel<8>, smem));
         decode_down_combine_kernel<8><<<grid, kp1 * 32, smem, s>>>(*a, h3, ldh, idx, score, logits, ld_logits, a->E,
                                                                    a->k, out);
     }

@@ -379,7 +379,7 @@ int launch_expert(const QeExpertArgs *a, const float *xin, int ldx, const QeBuck
     const size_t smem = sizeof(uint32_t) * (size_t)chunk * tstride + sizeof(float) * (size_t)kNT * (Kmax / GS);
     if (smem > 200 * 1024) QE_FAIL("expert kernel: K=%d needs %zu B of shared memory", Kmax, smem);
     auto kern = T <= kSplitMaxT ? expert_kernel<BITS, GS, MODE, kSplitK> : expert_kernel<BITS, GS, MODE, 1>;
-    QE_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    QE_CHECK(qe_set_smem((const void *)kern, smem));
     kern<<<grid, kWarps * 32, smem, s>>>(*a, xin, ldx, *b, T, out, ldo, chunk);
     QE_CHECK(cudaGetLastError());
     return 0;
@@ -480,7 +480,7 @@ int launch_qmat(const QeQDev *m, const float *x, int T, float *y, cudaStream_t s
     const size_t smem = sizeof(uint32_t) * (size_t)chunk * tstride + sizeof(float) * (size_t)kNT * ng;
     if (smem > 200 * 1024) QE_FAIL("qmat: cols=%d needs %zu B of shared memory", m->cols, smem);
     auto kern = qmat_kernel<BITS, GS>;
-    QE_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    QE_CHECK(qe_set_smem((const void *)kern, smem));
     dim3 grid((m->rows + kRowsPerCta - 1) / kRowsPerCta, (T + kNT - 1) / kNT);
     kern<<<grid, kWarps * 32, smem, s>>>(*m, x, T, y);
     QE_CHECK(cudaGetLastError());

@@ -24,6 +24,26 @@
     } while (0)
 
 static constexpr int QE_WARP = 32;
+
+/* Raise a kernel's dynamic shared-memory limit once per (kernel, device), and only above the 48 KB default:
+ * cudaFuncSetAttribute on every launch costs host time that a decode step cannot afford. */
+#include <mutex>
+#include <vector>
+inline cudaError_t qe_set_smem(const void *kern, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    struct Entry { const void *k; int dev; size_t bytes; };
+    static std::mutex mu;
+    static std::vector<Entry> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    for (auto &d : done)
+        if (d.k == kern && d.dev == dev && d.bytes >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) done.push_back({kern, dev, bytes});
+    return e;
+}
 static constexpr unsigned QE_FULL = 0xffffffffu;
 
 __device__ __forceinline__ float qe_bf16_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }

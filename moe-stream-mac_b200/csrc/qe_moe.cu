@@ -777,6 +777,95 @@ int qe_moe_forward_device(QeMoe *m, int T, const float *x, float *out, void *str
     return 0;
 }
 
+struct QeMoeGraph {
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+    void *ws;                      /* the graph's own scratch (the shared workspace may be reallocated) */
+    int device;
+    unsigned long long launches;   /* kernels in one replay */
+};
+
+}  // extern "C"
+
+namespace {
+/* qe_moe_forward_device on a given scratch workspace */
+int forward_ws(QeMoe *m, int T, const float *x, float *out, char *ws, int sms, cudaStream_t s) {
+    const int P = std::min(T, m->cfg.max_tokens);
+    Scratch sc;
+    scratch_layout(m->cfg, P, ws, &sc);
+    for (int t0 = 0; t0 < T; t0 += P) {
+        const int n = std::min(P, T - t0);
+        const size_t o = (size_t)t0 * m->cfg.hidden;
+        if (run_pass(m, x + o, out + o, n, sc, sms, s)) return -1;
+    }
+    return 0;
+}
+}  // namespace
+
+extern "C" {
+
+QeMoeGraph *qe_moe_graph_create(QeMoe *m, int T, const float *x, float *out) {
+    if (!m || !x || !out || T < 1 || m->cfg.ep_size > 1) {
+        fprintf(stderr, "qengine_b200: graph_create: bad arguments\n");
+        return nullptr;
+    }
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return nullptr;
+    cudaStream_t s = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    QeMoeGraph *g = (QeMoeGraph *)calloc(1, sizeof(QeMoeGraph));
+    bool ok = g != nullptr;
+    const size_t wsb = scratch_layout(m->cfg, std::min(T, m->cfg.max_tokens), nullptr, nullptr);
+    ok = ok && cudaMalloc(&g->ws, wsb) == cudaSuccess;
+    /* one eager forward first: kernel attributes set (that may not happen during capture) */
+    ok = ok && forward_ws(m, T, x, out, (char *)g->ws, d->sms, s) == 0 && cudaStreamSynchronize(s) == cudaSuccess;
+    const unsigned long long l0 = g_launches.load();
+    ok = ok && cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    if (ok) {
+        const int rc = forward_ws(m, T, x, out, (char *)g->ws, d->sms, s);
+        cudaGraph_t graph = nullptr;
+        const bool ended = cudaStreamEndCapture(s, &graph) == cudaSuccess;
+        ok = rc == 0 && ended;
+        if (ok) {
+            g->graph = graph;
+            ok = cudaGraphInstantiate(&g->exec, graph, 0) == cudaSuccess;
+        } else if (graph) {
+            cudaGraphDestroy(graph);
+        }
+    }
+    cudaStreamDestroy(s);
+    if (!ok) {
+        fprintf(stderr, "qengine_b200: graph_create: capture failed\n");
+        if (g) {
+            if (g->exec) cudaGraphExecDestroy(g->exec);
+            if (g->graph) cudaGraphDestroy(g->graph);
+            if (g->ws) cudaFree(g->ws);
+            free(g);
+        }
+        return nullptr;
+    }
+    g->device = m->device;
+    g->launches = g_launches.load() - l0;
+    return g;
+}
+
+int qe_moe_graph_launch(QeMoeGraph *g, void *stream) {
+    if (!g) QE_FAIL("graph_launch: null graph");
+    QE_CHECK(cudaSetDevice(g->device));
+    QE_CHECK(cudaGraphLaunch(g->exec, (cudaStream_t)stream));
+    g_launches += g->launches;
+    return 0;
+}
+
+void qe_moe_graph_free(QeMoeGraph *g) {
+    if (!g) return;
+    cudaSetDevice(g->device);
+    cudaGraphExecDestroy(g->exec);
+    cudaGraphDestroy(g->graph);
+    cudaFree(g->ws);
+    free(g);
+}
+
 int qe_moe_forward(QeMoe *m, int T, const float *x, float *out) {
     if (!m || !x || !out || T < 1) QE_FAIL("forward: bad arguments");
     if (m->cfg.ep_size > 1) QE_FAIL("forward: this handle holds experts [%d, %d) only: use the qe_moe_ep_* calls",

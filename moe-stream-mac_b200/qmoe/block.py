@@ -107,6 +107,10 @@ class MoeBlock:
         if lib().qe_moe_forward_device(self.handle, T, C.c_void_p(x_ptr), C.c_void_p(out_ptr), C.c_void_p(stream)):
             raise EngineError("qe_moe_forward_device failed")
 
+    def graph(self, T: int, x_ptr: int, out_ptr: int) -> "ForwardGraph":
+        """forward_device of T tokens on fixed device buffers, captured into a CUDA graph (qe_moe_graph_create)."""
+        return ForwardGraph(self, T, x_ptr, out_ptr)
+
     def route(self, x: np.ndarray):
         x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
         T = x.shape[0]
@@ -119,3 +123,28 @@ class MoeBlock:
     @property
     def weight_bytes(self) -> int:
         return lib().qe_moe_weight_bytes(self.handle)
+
+
+class ForwardGraph:
+    """A captured forward (include/qe_moe.h qe_moe_graph_*); launch() replays it on a stream."""
+
+    def __init__(self, block: MoeBlock, T: int, x_ptr: int, out_ptr: int):
+        self.block = block   # keeps the weights alive
+        self.handle = lib().qe_moe_graph_create(block.handle, T, C.c_void_p(x_ptr), C.c_void_p(out_ptr))
+        if not self.handle:
+            raise EngineError("qe_moe_graph_create failed")
+
+    def launch(self, stream: int = 0) -> None:
+        if lib().qe_moe_graph_launch(self.handle, C.c_void_p(stream)):
+            raise EngineError("qe_moe_graph_launch failed")
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib().qe_moe_graph_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -85,6 +85,10 @@ def lib() -> C.CDLL:
         L.qe_moe_ep_dispatch_p2p.argtypes = [vp, vp, C.c_int, vp, vp, vp, vp, vp]
         L.qe_moe_ep_experts_p2p.argtypes = [vp, vp, C.c_int, vp]
         L.qe_moe_ep_combine_p2p.argtypes = [vp, vp, C.c_int, vp, vp, vp, vp]
+        L.qe_moe_graph_create.restype = vp
+        L.qe_moe_graph_create.argtypes = [vp, C.c_int, vp, vp]
+        L.qe_moe_graph_launch.argtypes = [vp, vp]
+        L.qe_moe_graph_free.argtypes = [vp]
         L.qe_moe_open_safetensors.restype = vp
         L.qe_moe_open_safetensors.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(QeMoeConfig)]
         L.qe_safetensors_tensor_info.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(C.c_int64),

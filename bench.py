@@ -181,17 +181,22 @@ def profiled_traffic(kernel: str, config: str):
 
 
 def expert_kernel_name(cfg, stage: str, T: int) -> str:
-    """The kernel the library runs for this stage (tensor-core path for batches of 64 tokens or more when
-    the shape allows it: group size 64, every matrix a whole number of 128-row tiles)."""
+    """The kernel the library runs for this stage: decode GEMVs for up to 4 tokens, the tensor-core kernels for
+    larger batches (group size 64, every matrix a whole number of 128-row tiles), the grouped GEMVs when
+    selected (QE_EXPERT_PATH=group), mma.sync kernels otherwise."""
     path = os.environ.get("QE_EXPERT_PATH", "auto")
-    tc = (T >= 64 and cfg.group_size == 64 and all(d % 128 == 0 for d in (cfg.hidden, cfg.inter, cfg.sh_inter))
-          and path != "mma")
-    decode = (T <= 4 and cfg.group_size == 64 and cfg.inter == cfg.sh_inter and path == "auto"
-              and (cfg.hidden * cfg.bits // 8) % 1024 == 0 and (cfg.inter * cfg.bits // 8) % 128 == 0)
-    if tc:
-        return f"tc_expert_kernel<{cfg.bits},{2 if stage == 'gateup' else 1}>"
+    bh, bi = cfg.hidden * cfg.bits // 8, cfg.inter * cfg.bits // 8
+    tc = (T >= 5 and cfg.group_size == 64 and all(d % 128 == 0 for d in (cfg.hidden, cfg.inter, cfg.sh_inter))
+          and path in ("auto", "tc"))
+    decode = (T <= 4 and cfg.group_size == 64 and cfg.inter == cfg.sh_inter and path in ("auto", "gemv")
+              and bh % 128 == 0 and bh // 128 >= 8 and bi % 128 == 0)
+    group = path == "group" and cfg.group_size == 64 and bh % 64 == 0 and bh // 64 >= 4 and bi % 64 == 0
     if decode:
         return f"decode_gateup_kernel<{cfg.bits}>" if stage == "gateup" else f"decode_down_combine_kernel<{cfg.bits}>"
+    if group:
+        return f"group_gateup_kernel<{cfg.bits}>" if stage == "gateup" else f"group_down_kernel<{cfg.bits}>"
+    if tc:
+        return f"tc_expert_kernel<{cfg.bits},{2 if stage == 'gateup' else 1}>"
     return f"expert_kernel<{cfg.bits},{cfg.group_size},{stage}>"
 
 

@@ -63,6 +63,14 @@ int qe_launch_combine_sel_scatter(const float *ybuf, const int32_t *idx, const f
 /* Decode GEMVs (decode.cu): gate/up + SwiGLU per (token, slot) pair into h3 [T*(k+1)][ldh], then down + the
  * weighted combine (top-k order, then the gated shared expert) into out [T][hidden]. */
 bool qe_decode_supported(const QeExpertArgs *a);
+/* Expert-centric grouped GEMVs for batched decode (group_gemv.cu). */
+bool qe_group_supported(const QeExpertArgs *a);
+int qe_group_tokens(void);
+int qe_group_rows(void);
+int qe_launch_group_gateup(const QeExpertArgs *a, const float *x, const QeBuckets *b, int sms, float *h3, int ldh,
+                           cudaStream_t s);
+int qe_launch_group_down(const QeExpertArgs *a, const float *h3, int ldh, const QeBuckets *b, int sms, float *ybuf,
+                         cudaStream_t s);
 int qe_launch_decode_gateup(const QeExpertArgs *a, const float *x, const int32_t *idx, int T, float *h3, int ldh,
                             cudaStream_t s);
 int qe_launch_decode_down_combine(const QeExpertArgs *a, const float *h3, int ldh, const int32_t *idx,
@@ -83,15 +91,22 @@ int qe_launch_synth_normal(uint64_t seed, uint32_t block, uint32_t stream, size_
 int qe_num_sms(void);
 
 /* Tensor-core (tcgen05) prefill path, expert_tc.cu. */
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+/* Split activations of the tensor-core path: per group of 64 inputs, v * 2^e = hi + lo (fp16). */
+struct QeTcBufs {
+    __half *act;            /* gate/up input [2][T][hidden] */
+    float *actsum, *actinv; /* [T][hidden/64]: group sums of x, 2^-e */
+    __half *h3s;            /* down input [2][npairs][ldh] */
+    float *h3sum, *h3inv;   /* [npairs][ldh/64] */
+    int ldh;
+};
 bool qe_tc_supported(const QeExpertArgs *a);
 size_t qe_tc_map_bytes(void);
 int qe_tc_weight_maps(const QeQDev *q, int n_experts, void *codes_map, void *sc_map, void *bi_map);
 int qe_launch_tc_gateup(const QeExpertArgs *a, const void *maps, const float *x, const QeBuckets *b, int T,
-                        __nv_bfloat16 *act, float *actsum, __nv_bfloat16 *h3s, float *h3sum, int ldh, int grid,
-                        cudaStream_t s);
-int qe_launch_tc_down(const QeExpertArgs *a, const void *maps, const __nv_bfloat16 *h3s, const float *h3sum, int ldh,
-                      const QeBuckets *b, int T, float *ybuf, int grid, cudaStream_t s);
+                        const QeTcBufs *t, int grid, cudaStream_t s);
+int qe_launch_tc_down(const QeExpertArgs *a, const void *maps, const QeBuckets *b, int T, const QeTcBufs *t,
+                      float *ybuf, int grid, cudaStream_t s);
 int qe_tc_error(void);
 int qe_tc_bm(void);
 int qe_tc_bn(void);

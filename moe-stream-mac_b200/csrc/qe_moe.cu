@@ -25,9 +25,11 @@
 
 int qe_expert_rows_per_cta(int T);
 
-/* Batches of at least this many tokens take the tensor-core (tcgen05) expert path when the shape allows;
- * batches of at most kDecodeMaxTokens take the decode GEMVs (decode.cu); the mma.sync kernels take the rest. */
-static constexpr int kTcMinTokens = 64;
+/* Expert path by batch size (auto): at most kDecodeMaxTokens tokens take the decode GEMVs (decode.cu); larger
+ * batches the tensor-core (tcgen05) kernels when the shape allows (measured faster than the grouped GEMVs of
+ * group_gemv.cu and the mma.sync kernels from 8 tokens up, on the 4-bit and 8-bit benchmark blocks); shapes
+ * neither covers take the mma.sync kernels. The grouped GEMVs run when selected (QE_EXPERT_PATH=group). */
+static constexpr int kTcMinTokens = 5;
 static constexpr int kDecodeMaxTokens = 4;
 
 /* ------------------------------------------------------------------ per-device context and workspace */
@@ -117,8 +119,7 @@ struct Scratch {
     float *rpart;               /* fp32 router chunk values [hidden/64][T][E+1] (prefill GEMM) */
     int32_t *idx;
     QeBuckets b;
-    __nv_bfloat16 *act, *h3s;   /* tensor-core path: split activations [3][npairs][K] */
-    float *actsum, *h3sum;      /* per-(pair, group of 64) sums */
+    QeTcBufs tcb;               /* tensor-core path: split activations, group sums, unscale factors */
 };
 
 size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
@@ -146,10 +147,13 @@ size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
     t.b.slot_expert = (int32_t *)take(sizeof(int32_t) * (E + 2));
     t.b.slot_items = (int32_t *)take(sizeof(int32_t) * 2 * (E + 2));
     t.b.n_active = (int32_t *)take(sizeof(int32_t) * 4);
-    t.act = (__nv_bfloat16 *)take(2 * 3 * npair * c.hidden);
-    t.actsum = (float *)take(4 * npair * (c.hidden / 64 + 1));
-    t.h3s = (__nv_bfloat16 *)take(2 * 3 * npair * I);
-    t.h3sum = (float *)take(4 * npair * (I / 64 + 1));
+    t.tcb.act = (__half *)take(2 * 2 * (size_t)T * c.hidden);
+    t.tcb.actsum = (float *)take(4 * (size_t)T * (c.hidden / 64 + 1));
+    t.tcb.actinv = (float *)take(4 * (size_t)T * (c.hidden / 64 + 1));
+    t.tcb.h3s = (__half *)take(2 * 2 * npair * I);
+    t.tcb.h3sum = (float *)take(4 * npair * (I / 64 + 1));
+    t.tcb.h3inv = (float *)take(4 * npair * (I / 64 + 1));
+    t.tcb.ldh = I;
     if (s) *s = t;
     return off;
 }
@@ -169,9 +173,10 @@ struct QeMoe {
     QeExpertArgs ex;
     size_t expert_bytes;    /* bytes of one routed expert (gate+up+down codes, scales, biases) */
     int e0, E_loc;          /* routed experts held here: global ids [e0, e0 + E_loc) (expert parallelism) */
-    int path;               /* 0 = auto, 1 = mma.sync only, 2 = tensor-core (tcgen05) whenever supported */
+    int path;               /* 0 = auto, 1 = mma.sync, 2 = tensor-core (tcgen05), 3 = decode GEMVs, 4 = grouped GEMVs */
     bool tc;                /* tensor-core path available for this shape */
     bool decode;            /* decode GEMVs available for this shape */
+    bool group;             /* grouped GEMVs available for this shape */
     alignas(64) unsigned char maps_gu[2 * 2 * 3 * 128];  /* [routed/shared][gate/up][codes, scales, biases] */
     alignas(64) unsigned char maps_dn[2 * 3 * 128];      /* [routed/shared][codes, scales, biases] */
 };
@@ -261,8 +266,10 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     m->ex.E = El; m->ex.k = c->top_k; m->ex.hidden = H; m->ex.inter = I; m->ex.sh_inter = Is;
     size_t wb, gb;
     m->expert_bytes = qbytes(1, I, H, b, gs, &wb, &gb) * 2 + qbytes(1, H, I, b, gs, &wb, &gb);
-    const char *path = getenv("QE_EXPERT_PATH");   /* auto (default) | mma | tc | gemv */
-    m->path = path && !strcmp(path, "mma") ? 1 : path && !strcmp(path, "tc") ? 2 : path && !strcmp(path, "gemv") ? 3 : 0;
+    const char *path = getenv("QE_EXPERT_PATH");   /* auto (default) | mma | tc | gemv | group */
+    m->path = path && !strcmp(path, "mma") ? 1 : path && !strcmp(path, "tc") ? 2 : path && !strcmp(path, "gemv") ? 3
+            : path && !strcmp(path, "group") ? 4 : 0;
+    m->group = qe_group_supported(&m->ex);
     m->tc = qe_tc_supported(&m->ex);
     m->decode = qe_decode_supported(&m->ex);
     if (m->tc) {
@@ -517,6 +524,23 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
         g_launches += 2;
         return 0;
     }
+    const bool use_group = m->group && m->path == 4;
+    if (use_group) {
+        /* batched decode: every active expert's rows streamed once per chunk of its tokens */
+        const int R = qe_group_rows(), NB = qe_group_tokens();
+        const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
+                  tiles_dn = (c.hidden + R - 1) / R;
+        if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s)) return -1;
+        prof_mark(dev, s);
+        if (qe_launch_group_gateup(&m->ex, x, &sc.b, sms, sc.h3, I, s)) return -1;
+        prof_mark(dev, s);
+        if (qe_launch_group_down(&m->ex, sc.h3, I, &sc.b, sms, sc.ybuf, s)) return -1;
+        prof_mark(dev, s);
+        if (qe_launch_combine(sc.ybuf, sc.score, sc.logits, c.E + 1, T, c.E, c.top_k, c.hidden, out, s)) return -1;
+        prof_mark(dev, s);
+        g_launches += 4;
+        return 0;
+    }
     const bool use_tc = m->tc && (m->path == 2 || (m->path == 0 && T >= kTcMinTokens));
     if (use_tc) {
         const int R = qe_tc_bm(), NB = qe_tc_bn();
@@ -524,10 +548,9 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
                   tiles_dn = (c.hidden + R - 1) / R;
         if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s)) return -1;
         prof_mark(dev, s);
-        if (qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, T, sc.act, sc.actsum, sc.h3s, sc.h3sum, I, sms, s))
-            return -1;
+        if (qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, T, &sc.tcb, sms, s)) return -1;
         prof_mark(dev, s);
-        if (qe_launch_tc_down(&m->ex, m->maps_dn, sc.h3s, sc.h3sum, I, &sc.b, T, sc.ybuf, sms, s)) return -1;
+        if (qe_launch_tc_down(&m->ex, m->maps_dn, &sc.b, T, &sc.tcb, sc.ybuf, sms, s)) return -1;
         prof_mark(dev, s);
         if (qe_launch_combine(sc.ybuf, sc.score, sc.logits, c.E + 1, T, c.E, c.top_k, c.hidden, out, s)) return -1;
         prof_mark(dev, s);
@@ -673,14 +696,24 @@ int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sm
     const int El = m->E_loc, k = c.top_k;
     const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
     const int sh_tokens = shared ? n : 0;
-    const bool use_tc = m->tc && (m->path == 2 || (m->path == 0 && n >= kTcMinTokens));
-    if (use_tc) {
+    const bool use_group = m->group && m->path == 4;
+    const bool use_tc = !use_group && m->tc && (m->path == 2 || (m->path == 0 && n >= kTcMinTokens));
+    if (use_group) {
+        const int R = qe_group_rows(), NB = qe_group_tokens();
+        const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
+                  tiles_dn = (c.hidden + R - 1) / R;
+        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s) ||
+            qe_launch_group_gateup(&m->ex, x, &sc.b, sms, sc.h3, I, s) ||
+            qe_launch_group_down(&m->ex, sc.h3, I, &sc.b, sms, sc.ybuf, s))
+            return -1;
+        g_launches += 3;
+    } else if (use_tc) {
         const int R = qe_tc_bm(), NB = qe_tc_bn();
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
                   tiles_dn = (c.hidden + R - 1) / R;
         if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s) ||
-            qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, n, sc.act, sc.actsum, sc.h3s, sc.h3sum, I, sms, s) ||
-            qe_launch_tc_down(&m->ex, m->maps_dn, sc.h3s, sc.h3sum, I, &sc.b, n, sc.ybuf, sms, s))
+            qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, n, &sc.tcb, sms, s) ||
+            qe_launch_tc_down(&m->ex, m->maps_dn, &sc.b, n, &sc.tcb, sc.ybuf, sms, s))
             return -1;
         g_launches += 4;
     } else {

@@ -119,10 +119,21 @@ struct RowStream {
 };
 
 /* n vectors of K floats into shared memory (vs[j*K + c]) and their sums per group of 64 (gs[j*(K/64) + g]):
- * one warp per group, a fixed shuffle tree. src(j) gives vector j's global address. */
+ * 16-byte copies (K a multiple of 4, rows 16-byte aligned), then one warp per group, a fixed shuffle tree.
+ * src(j) gives vector j's global address. */
 template <typename Src>
 __device__ void stage_vecs(Src src, int n, int K, float *vs, float *gs) {
-    for (int i = threadIdx.x; i < n * K; i += blockDim.x) vs[i] = src(i / K)[i % K];
+    const int k4 = K >> 2;
+    int j = 0, c = threadIdx.x;   /* element c of vector j, advanced without divisions */
+    while (true) {
+        while (c >= k4 && j < n) {
+            c -= k4;
+            j++;
+        }
+        if (j >= n) break;
+        reinterpret_cast<float4 *>(vs)[(size_t)j * k4 + c] = __ldg(reinterpret_cast<const float4 *>(src(j)) + c);
+        c += blockDim.x;
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5, ng = K / kGS;
     for (int i = warp; i < n * ng; i += nw) {
@@ -239,7 +250,7 @@ bool qe_decode_supported(const QeExpertArgs *a) {
     if (a->gate.group_size != kGS || (bits != 4 && bits != 8)) return false;
     if (a->inter != a->sh_inter || a->k > 16) return false;
     const int bh = a->hidden * bits / 8, bi = a->inter * bits / 8;
-    return bh % kChunk == 0 && bh / kChunk >= kParts && bi % kChunk == 0;
+    return bh % kChunk == 0 && bh / kChunk >= kParts && bi % kChunk == 0 && a->inter % 4 == 0;
 }
 
 int qe_launch_decode_gateup(const QeExpertArgs *a, const float *x, const int32_t *idx, int T, float *h3, int ldh,

@@ -200,6 +200,14 @@ def expert_kernel_name(cfg, stage: str, T: int) -> str:
     return f"expert_kernel<{cfg.bits},{cfg.group_size},{stage}>"
 
 
+def fused_decode(cfg, T: int) -> bool:
+    """Whether the library runs the decode step as one cooperative launch (decode_fused_kernel): with
+    QE_DECODE_FUSED=1, for decode GEMV shapes, up to 4 tokens, fp32 router, top_k <= 15."""
+    if os.environ.get("QE_DECODE_FUSED", "0") != "1" or os.environ.get("QE_EXPERT_PATH", "auto") not in ("auto", "gemv"):
+        return False
+    return expert_kernel_name(cfg, "gateup", T).startswith("decode_") and cfg.top_k <= 15
+
+
 def stage_bytes(cfg, uniq: int, T: int) -> dict:
     """Algorithmic bytes per launch of each expert kernel: every active expert's weights once, plus the
     activations the kernel must read and write (fp32)."""
@@ -398,13 +406,22 @@ def main():
         idx, _ = blocks[0].route(x.cpu().numpy())
         uniq = len(np.unique(idx))
         sb = stage_bytes(cfg, uniq, T)
-        top = max(("gateup", "down"), key=lambda s: stage_ms[s])
+        total_stage = sum(stage_ms.values())
+        if fused_decode(cfg, T):
+            # fused decode step: one kernel (router, top-k, gate/up, down + combine); its compulsory bytes are
+            # the router, every selected expert and the shared expert once, x in and out back
+            top = "router"
+            sb = {"router": 4 * (cfg.E + 1) * cfg.hidden + uniq * cfg.expert_bytes + cfg.shared_bytes
+                  + 8 * T * cfg.hidden}
+            kname, kdesc = f"decode_fused_kernel<{cfg.bits}>", " (whole decode step, one cooperative launch)"
+        else:
+            top = max(("gateup", "down"), key=lambda s: stage_ms[s])
+            kname = expert_kernel_name(cfg, top, T)
+            kdesc = " (gate/up + SwiGLU)" if top == "gateup" else " (down)"
         per_launch_ms = stage_ms[top] / max(passes, 1)
         achieved = sb[top] / (per_launch_ms / 1e3) / 1e9
-        total_stage = sum(stage_ms.values())
-        kname = expert_kernel_name(cfg, top, T)
         tr = profiled_traffic(kname, cfg.name)
-        roofline = {"bound": "hbm", "kernel": kname + (" (gate/up + SwiGLU)" if top == "gateup" else " (down)"),
+        roofline = {"bound": "hbm", "kernel": kname + kdesc,
                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                     "traffic": tr[0] if tr else None,
                     "traffic_source": f"ncu dram__bytes_read.sum + dram__bytes_write.sum, profiles/{tr[1]}" if tr

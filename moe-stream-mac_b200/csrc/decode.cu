@@ -19,12 +19,23 @@
  * 2 of the 24 bits). Then scale * sum_q + bias * sum_x per group (qmat.c:43), groups in order. fp32 throughout;
  * the order differs from the reference's (tolerance 1e-5 rel-L2).
  */
+#include <algorithm>
+
 #include "qe_common.cuh"
 #include "qe_kernels.h"
+#include "route_dev.cuh"
 
 namespace {
 
 constexpr int kGS = 64;
+constexpr int kFusedMaxTokens = 4;   /* tokens of a fused decode step (kDecodeMaxTokens in qe_moe.cu) */
+#define QE_DECODE_WAIT_NS 2000000000ull
+
+__device__ __forceinline__ uint64_t decode_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 /* Code q as the float 1 + q/16 (4-bit) or 1 + q/256 (8-bit): the code's bits are the top mantissa bits, one
  * shift and one logic op. */
@@ -173,22 +184,24 @@ __device__ __forceinline__ QRow qrow(const QeQDev &m, int e, int row) {
 }
 
 constexpr int kParts = 8;   /* K parts per matrix in the gate/up kernel */
+constexpr int kGuThreads = 2 * kParts * 32;
 
+/* Gate/up + SwiGLU of one (token-slot pair p, 32-row block at r0): warps 0-7 stream the gate rows, 8-15 the up
+ * rows, each warp one eighth of K; parts summed in order, h = silu(g) * u -> h3[p][r0 + lane]. idx: the top-k
+ * ids [T][k] (global or shared memory). All 512 threads of the CTA call it; xs: hidden + hidden/64 floats of
+ * shared memory. */
 template <int BITS>
-__global__ void __launch_bounds__(2 * kParts * 32) decode_gateup_kernel(QeExpertArgs a, const float *__restrict__ x,
-                                                                        const int32_t *__restrict__ idx, int k,
-                                                                        float *__restrict__ h3, int ldh) {
-    extern __shared__ __align__(16) float smem[];
-    __shared__ float part_sum[2 * kParts][32];
-    const int p = blockIdx.x;                 /* pair t*(k+1) + j */
+__device__ __forceinline__ void gateup_unit(const QeExpertArgs &a, const float *__restrict__ x, const int32_t *idx,
+                                            int k, float *__restrict__ h3, int ldh, int p, int r0, float *xs,
+                                            float (*part_sum)[32]) {
     const int t = p / (k + 1), j = p % (k + 1);
     const bool shared = j == k;
-    const int e = shared ? 0 : idx[(size_t)t * k + j];
+    const int e = shared ? 0 : idx[t * k + j];
     const QeQDev &G = shared ? a.sh_gate : a.gate, &U = shared ? a.sh_up : a.up;
     const int rows = G.rows, K = G.cols;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m = warp / kParts, part = warp % kParts;
-    const int r0 = blockIdx.y * 32, row = min(r0 + lane, rows - 1);
+    const int row = min(r0 + lane, rows - 1);
     const int nch = K * BITS / 8 / kChunk;
     const QRow q = qrow(m ? U : G, e, row);
     RowStream<BITS> st;
@@ -196,7 +209,7 @@ __global__ void __launch_bounds__(2 * kParts * 32) decode_gateup_kernel(QeExpert
     st.c0 = part * nch / kParts;
     st.c1 = (part + 1) * nch / kParts;
     st.start();                               /* codes in flight while x is staged */
-    float *xs = smem, *gsum = smem + K;
+    float *gsum = xs + K;
     stage_vecs([&](int) { return x + (size_t)t * K; }, 1, K, xs, gsum);
     part_sum[warp][lane] = st.finish(xs, gsum);
     __syncthreads();
@@ -211,6 +224,54 @@ __global__ void __launch_bounds__(2 * kParts * 32) decode_gateup_kernel(QeExpert
 }
 
 template <int BITS>
+__global__ void __launch_bounds__(kGuThreads) decode_gateup_kernel(QeExpertArgs a, const float *__restrict__ x,
+                                                                   const int32_t *__restrict__ idx, int k,
+                                                                   float *__restrict__ h3, int ldh) {
+    extern __shared__ __align__(16) float smem[];
+    __shared__ float part_sum[2 * kParts][32];
+    gateup_unit<BITS>(a, x, idx, k, h3, ldh, blockIdx.x, blockIdx.y * 32, smem, part_sum);
+}
+
+/* Down projection of token t's k+1 slots for the 32 output rows at r0, combined in slot order: warp j < k+1
+ * streams slot j's down rows (k routed experts, then the shared one). begin() requests the codes; end() stages
+ * the token's k+1 activation vectors (shared memory hs: (k+1) * (K + K/64) floats), finishes the dots and
+ * writes out = sum_j score_j y_j (slot order) + sigmoid(gate logit) y_shared (moe_layer.c:79-88). */
+template <int BITS>
+struct DownUnit {
+    RowStream<BITS> st;
+    int t, r0;
+    __device__ __forceinline__ void begin(const QeExpertArgs &a, const int32_t *idx, int k, int t_, int r0_) {
+        t = t_;
+        r0 = r0_;
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const int H = a.hidden, row = min(r0 + lane, H - 1);
+        st.c0 = 0;
+        st.c1 = 0;
+        if (warp > k) return;
+        const QRow q = warp == k ? qrow(a.sh_down, 0, row) : qrow(a.down, idx[t * k + warp], row);
+        st.row = q.codes; st.sc = q.sc; st.bi = q.bi; st.gstride = q.gstride;
+        st.c1 = a.down.cols * BITS / 8 / kChunk;
+        st.start();
+    }
+    __device__ __forceinline__ void end(const QeExpertArgs &a, const float *__restrict__ h3, int ldh, int k,
+                                        const float *score, const float *__restrict__ logits, int ld_logits,
+                                        float *__restrict__ out, float *hs, float (*ys)[32]) {
+        const int kp1 = k + 1, K = a.down.cols, H = a.hidden;
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        float *gsum = hs + (size_t)kp1 * K;
+        stage_vecs([&](int jj) { return h3 + ((size_t)t * kp1 + jj) * ldh; }, kp1, K, hs, gsum);
+        if (warp <= k) ys[warp][lane] = st.finish(hs + (size_t)warp * K, gsum + (size_t)warp * (K / kGS));
+        __syncthreads();
+        if (warp == 0 && r0 + lane < H) {
+            float o = 0.0f;
+            for (int jj = 0; jj < k; jj++) o = __fadd_rn(o, __fmul_rn(score[t * k + jj], ys[jj][lane]));
+            o = __fadd_rn(o, __fmul_rn(qe_sigmoid(logits[(size_t)t * ld_logits + a.E]), ys[k][lane]));
+            out[(size_t)t * H + r0 + lane] = o;
+        }
+    }
+};
+
+template <int BITS>
 __global__ void __launch_bounds__(17 * 32) decode_down_combine_kernel(QeExpertArgs a, const float *__restrict__ h3,
                                                                       int ldh, const int32_t *__restrict__ idx,
                                                                       const float *__restrict__ score,
@@ -218,26 +279,117 @@ __global__ void __launch_bounds__(17 * 32) decode_down_combine_kernel(QeExpertAr
                                                                       int E, int k, float *__restrict__ out) {
     extern __shared__ __align__(16) float smem[];
     __shared__ float ys[17][32];
-    const int t = blockIdx.x;
-    const int kp1 = k + 1;
-    const int K = a.down.cols, H = a.hidden;   /* the shared expert's down has the same K (checked at launch) */
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;   /* warp = slot */
-    const int r0 = blockIdx.y * 32, row = min(r0 + lane, H - 1);
-    const QRow q = warp == k ? qrow(a.sh_down, 0, row) : qrow(a.down, idx[(size_t)t * k + warp], row);
-    RowStream<BITS> st;
-    st.row = q.codes; st.sc = q.sc; st.bi = q.bi; st.gstride = q.gstride;
-    st.c0 = 0;
-    st.c1 = K * BITS / 8 / kChunk;
-    st.start();                               /* codes in flight while the activations are staged */
-    float *hs = smem, *gsum = smem + (size_t)kp1 * K;
-    stage_vecs([&](int jj) { return h3 + ((size_t)t * kp1 + jj) * ldh; }, kp1, K, hs, gsum);
-    ys[warp][lane] = st.finish(hs + (size_t)warp * K, gsum + (size_t)warp * (K / kGS));
+    (void)E;
+    DownUnit<BITS> du;
+    du.begin(a, idx, k, blockIdx.x, blockIdx.y * 32);   /* codes in flight while the activations are staged */
+    du.end(a, h3, ldh, k, score, logits, ld_logits, out, smem, ys);
+}
+
+/* ------------------------------------------------------------------ fused decode step */
+
+__device__ int g_decode_error;   /* first grid-barrier timeout code, read by qe_decode_error() */
+
+/* Grid-wide barrier of a cooperative launch (every CTA resident): arrive on bar[0], the last arrival resets it
+ * and advances the generation bar[1]; waiters poll the generation for at most QE_WAIT_NS. Returns false (and
+ * records `code`) on timeout. Every thread of the CTA calls it. */
+__device__ bool grid_sync(unsigned *bar, int code, int *ok_s) {
     __syncthreads();
-    if (warp == 0 && r0 + lane < H) {
-        float o = 0.0f;
-        for (int jj = 0; jj < k; jj++) o = __fadd_rn(o, __fmul_rn(score[(size_t)t * k + jj], ys[jj][lane]));
-        o = __fadd_rn(o, __fmul_rn(qe_sigmoid(logits[(size_t)t * ld_logits + E]), ys[k][lane]));
-        out[(size_t)t * H + r0 + lane] = o;
+    if (threadIdx.x == 0) {
+        volatile unsigned *gen = bar + 1;
+        const unsigned g = *gen;
+        __threadfence();
+        int ok = 1;
+        if (atomicAdd(bar, 1u) + 1u == gridDim.x) {
+            atomicExch(bar, 0u);
+            __threadfence();
+            atomicAdd(bar + 1, 1u);
+        } else {
+            const uint64_t t0 = decode_timer_ns();
+            while (*gen == g) {
+                if (decode_timer_ns() - t0 > QE_DECODE_WAIT_NS) {
+                    ok = 0;
+                    atomicCAS(&g_decode_error, 0, code);
+                    break;
+                }
+            }
+        }
+        __threadfence();
+        *ok_s = ok;
+    }
+    __syncthreads();
+    return *ok_s != 0;
+}
+
+struct FusedArgs {
+    QeExpertArgs a;
+    const float *W, *bias;      /* fp32 router [E+1][hidden] (row E: shared-expert gate), bias [E] or null */
+    const float *x;             /* [T][hidden] */
+    int T, vec;
+    float *logits;              /* [T][E+1] */
+    int32_t *idx;               /* [T][k] (written by CTA 0) */
+    float *score;               /* [T][k] (written by CTA 0) */
+    float *h3;                  /* [T*(k+1)][ldh] */
+    int ldh;
+    float *out;                 /* [T][hidden] */
+    unsigned *bar;              /* [2] grid barrier, zero at launch */
+};
+
+/* One decode step in one cooperative launch (one CTA of 512 threads per SM):
+ *   1. router logits: one warp per router row (route_dev.cuh), rows spread over every warp of the grid;
+ *   2. grid barrier; every CTA computes the softmax/top-k of each token itself (warp t: token t; identical
+ *      code and inputs, so identical results) into shared memory, CTA 0 also to idx/score;
+ *   3. gate/up + SwiGLU units (token-slot pair, 32 rows) spread over the CTAs; each CTA then requests the codes
+ *      of its first down unit (the slots' experts are known from step 2);
+ *   4. grid barrier (h3 complete); down + combine units (token, 32 output rows).
+ * Each phase's work is the standalone kernels' (router_gemv_f32_kernel, route_topk_kernel, decode_gateup_kernel,
+ * decode_down_combine_kernel), so the results are bit-identical to the four-launch path. */
+template <int BITS>
+__global__ void __launch_bounds__(kGuThreads, 1) decode_fused_kernel(const __grid_constant__ FusedArgs f) {
+    extern __shared__ __align__(16) float smem[];
+    __shared__ float part_sum[2 * kParts][32];
+    __shared__ int32_t s_idx[kFusedMaxTokens * 16];
+    __shared__ float s_score[kFusedMaxTokens * 16];
+    __shared__ int ok_s;
+    const QeExpertArgs &a = f.a;
+    const int E = a.E, k = a.k, kp1 = k + 1, T = f.T, H = a.hidden, I = a.inter;
+    const int warp = threadIdx.x >> 5;
+    constexpr int kWarps = kGuThreads / 32;
+    /* 1. router: row r on warp r / gridDim.x of CTA r % gridDim.x (every SM streams its share) */
+    for (int row = warp * gridDim.x + blockIdx.x; row <= E; row += gridDim.x * kWarps)
+        router_row_f32(f.W, f.bias, f.x, T, H, E, row, f.logits, f.vec);
+    if (!grid_sync(f.bar, 1, &ok_s)) return;
+    /* 2. top-k, per CTA */
+    if (warp < T) {
+        float *probs_s = smem + (size_t)warp * 2 * E;
+        int *idx_s = reinterpret_cast<int *>(probs_s + E);
+        route_topk_warp(f.logits + (size_t)warp * (E + 1), warp, E, k, probs_s, idx_s,
+                        blockIdx.x == 0 ? f.idx : s_idx, blockIdx.x == 0 ? f.score : s_score, nullptr);
+    }
+    __syncthreads();
+    if (blockIdx.x == 0) {   /* CTA 0 wrote to global memory: copy to its shared arrays */
+        for (int i = threadIdx.x; i < T * k; i += blockDim.x) {
+            s_idx[i] = f.idx[i];
+            s_score[i] = f.score[i];
+        }
+        __syncthreads();
+    }
+    /* 3. gate/up + SwiGLU */
+    const int nrb = I / 32, units3 = T * kp1 * nrb;
+    for (int u = blockIdx.x; u < units3; u += gridDim.x) {
+        gateup_unit<BITS>(a, f.x, s_idx, k, f.h3, f.ldh, u / nrb, (u % nrb) * 32, smem, part_sum);
+        __syncthreads();   /* shared memory is restaged by the next unit */
+    }
+    /* 4. down + combine; the first unit's codes are requested before the barrier */
+    const int nrd = H / 32, units4 = T * nrd;
+    float (*ys)[32] = part_sum;
+    DownUnit<BITS> du;
+    int u = blockIdx.x;
+    if (u < units4) du.begin(a, s_idx, k, u / nrd, (u % nrd) * 32);
+    if (!grid_sync(f.bar, 2, &ok_s)) return;
+    for (; u < units4; u += gridDim.x) {
+        if (u != (int)blockIdx.x) du.begin(a, s_idx, k, u / nrd, (u % nrd) * 32);
+        du.end(a, f.h3, f.ldh, k, s_score, f.logits, E + 1, f.out, smem, ys);
+        __syncthreads();
     }
 }
 
@@ -285,4 +437,49 @@ int qe_launch_decode_down_combine(const QeExpertArgs *a, const float *h3, int ld
     }
     QE_CHECK(cudaGetLastError());
     return 0;
+}
+
+/* The fused decode step (decode_fused_kernel): fp32 router, T <= kFusedMaxTokens tokens, at most 15 routed
+ * slots. Returns 1 (nothing launched) when the shape or the device does not allow it, 0 when launched, -1 on
+ * error. bar: two unsigned words of device memory, zeroed here before the launch. */
+int qe_launch_decode_fused(const QeExpertArgs *a, const float *W, const float *bias, const float *x, int T,
+                           float *logits, int32_t *idx, float *score, float *h3, int ldh, float *out, unsigned *bar,
+                           int sms, cudaStream_t s) {
+    const int E = a->E, k = a->k, H = a->hidden, I = a->inter;
+    if (!qe_decode_supported(a) || T < 1 || T > kFusedMaxTokens || k + 1 > 2 * kParts || E > 32 * kMaxEPL ||
+        H > 32 * kRouterLaneChunks * kRouterChunk || H % 32 || I % 32 || k > E)
+        return 1;
+    const int vec = H % 4 == 0 && ((uintptr_t)W | (uintptr_t)x) % 16 == 0;
+    size_t smem = sizeof(float) * (size_t)T * 2 * E;
+    smem = std::max(smem, sizeof(float) * ((size_t)H + H / kGS));
+    smem = std::max(smem, sizeof(float) * (size_t)(k + 1) * ((size_t)I + I / kGS));
+    if (smem > 200 * 1024) return 1;
+    const void *kern = a->gate.bits == 4 ? (const void *)decode_fused_kernel<4> : (const void *)decode_fused_kernel<8>;
+    QE_CHECK(qe_set_smem(kern, smem));
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGuThreads, smem) != cudaSuccess || per_sm < 1)
+        return 1;
+    FusedArgs f;
+    f.a = *a; f.W = W; f.bias = bias; f.x = x; f.T = T; f.vec = vec; f.logits = logits; f.idx = idx;
+    f.score = score; f.h3 = h3; f.ldh = ldh; f.out = out; f.bar = bar;
+    QE_CHECK(cudaMemsetAsync(bar, 0, 2 * sizeof(unsigned), s));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms);   /* one CTA per SM, all resident (cooperative) */
+    cfg.blockDim = dim3(kGuThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (a->gate.bits == 4) QE_CHECK(cudaLaunchKernelEx(&cfg, decode_fused_kernel<4>, f));
+    else QE_CHECK(cudaLaunchKernelEx(&cfg, decode_fused_kernel<8>, f));
+    return 0;
+}
+
+int qe_decode_error(void) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_decode_error, sizeof(int)) != cudaSuccess) return -1;
+    return v;
 }

@@ -59,11 +59,13 @@ __device__ __forceinline__ float qe_bf16_to_f32(uint16_t h) { return __uint_as_f
  * evaluates the argument reduction and the polynomial with fused multiply-adds; this function does
  * the same with DFMA. The 2^(i/32) table was computed here to 60 significant digits and rounded to
  * double; the polynomial coefficients are the method's published minimax constants.
- * tests/test_expf_gpu.py compares it with the host expf over every negative float and every float in
+ * tests/test_gpu_kernels.py compares it with the host expf over every negative float and every float in
  * [0, 88.72]; the same comparison on the CPU (this formula in C, with fma()) gave 0 mismatches over all
  * 2.1e9 negative floats.
  * ------------------------------------------------------------------------------------------------- */
-__constant__ unsigned long long qe_exp2_tab[32] = {
+/* In global memory (read through the read-only cache): the lanes of a warp index it differently, which
+ * constant memory would serialise; 256 bytes, so a warp's lookups hit one or two L1 lines. */
+__device__ const unsigned long long qe_exp2_tab[32] = {
     0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
     0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
     0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
@@ -79,22 +81,25 @@ __device__ __forceinline__ float qe_expf(float x) {
     const double kC0 = 0x1.c6af84b912394p-5 / (32.0 * 32.0 * 32.0);
     const double kC1 = 0x1.ebfce50fac4f3p-3 / (32.0 * 32.0);
     const double kC2 = 0x1.62e42ff0c52d6p-1 / 32.0;
-    if (x != x) return x + x;                                   /* NaN */
-    if (x < -0x1.9fe368p6f) return 0.0f;                        /* underflows to 0 (and -inf) */
-    if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);   /* overflow */
+    /* branch-free: the main path is evaluated for every x (no input traps; results outside the range are
+     * replaced below), so independent calls overlap */
     const double xd = (double)x;
     double kd = __fma_rn(kInvLn2N, xd, kShift);
     const unsigned long long ki = (unsigned long long)__double_as_longlong(kd);
     kd = __dsub_rn(kd, kShift);
     const double r = __fma_rn(kInvLn2N, xd, -kd);
-    const unsigned long long t = qe_exp2_tab[ki & 31ull] + (ki << 47);
+    const unsigned long long t = __ldg(qe_exp2_tab + (ki & 31ull)) + (ki << 47);
     const double s = __longlong_as_double((long long)t);
     const double z = __fma_rn(kC0, r, kC1);
     const double r2 = __dmul_rn(r, r);
     double y = __fma_rn(kC2, r, 1.0);
     y = __fma_rn(z, r2, y);
     y = __dmul_rn(y, s);
-    return __double2float_rn(y);
+    float res = __double2float_rn(y);
+    res = x > 0x1.62e42ep6f ? __int_as_float(0x7f800000) : res;   /* overflow */
+    res = x < -0x1.9fe368p6f ? 0.0f : res;                         /* underflows to 0 (and -inf) */
+    res = x != x ? x + x : res;                                     /* NaN */
+    return res;
 }
 
 /* silu(g) * u exactly as engine/src/ops.c:16-21 evaluates it: g / (1 + expf(-g)) * u. */

@@ -63,6 +63,10 @@ int qe_launch_combine_sel_scatter(const float *ybuf, const int32_t *idx, const f
 /* Decode GEMVs (decode.cu): gate/up + SwiGLU per (token, slot) pair into h3 [T*(k+1)][ldh], then down + the
  * weighted combine (top-k order, then the gated shared expert) into out [T][hidden]. */
 bool qe_decode_supported(const QeExpertArgs *a);
+int qe_launch_decode_fused(const QeExpertArgs *a, const float *W, const float *bias, const float *x, int T,
+                           float *logits, int32_t *idx, float *score, float *h3, int ldh, float *out, unsigned *bar,
+                           int sms, cudaStream_t s);
+int qe_decode_error(void);
 /* Expert-centric grouped GEMVs for batched decode (group_gemv.cu). */
 bool qe_group_supported(const QeExpertArgs *a);
 int qe_group_tokens(void);

@@ -120,6 +120,7 @@ struct Scratch {
     int32_t *idx;
     QeBuckets b;
     QeTcBufs tcb;               /* tensor-core path: split activations, group sums, unscale factors */
+    unsigned *gbar;             /* grid barrier of the fused decode kernel */
 };
 
 size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
@@ -154,6 +155,7 @@ size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
     t.tcb.h3sum = (float *)take(4 * npair * (I / 64 + 1));
     t.tcb.h3inv = (float *)take(4 * npair * (I / 64 + 1));
     t.tcb.ldh = I;
+    t.gbar = (unsigned *)take(2 * sizeof(unsigned));
     if (s) *s = t;
     return off;
 }
@@ -177,6 +179,8 @@ struct QeMoe {
     bool tc;                /* tensor-core path available for this shape */
     bool decode;            /* decode GEMVs available for this shape */
     bool group;             /* grouped GEMVs available for this shape */
+    bool fused;             /* decode steps as one cooperative launch (QE_DECODE_FUSED=1; measured slower than
+                             * the four launches replayed from a CUDA graph, so off by default) */
     alignas(64) unsigned char maps_gu[2 * 2 * 3 * 128];  /* [routed/shared][gate/up][codes, scales, biases] */
     alignas(64) unsigned char maps_dn[2 * 3 * 128];      /* [routed/shared][codes, scales, biases] */
 };
@@ -270,6 +274,8 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     m->path = path && !strcmp(path, "mma") ? 1 : path && !strcmp(path, "tc") ? 2 : path && !strcmp(path, "gemv") ? 3
             : path && !strcmp(path, "group") ? 4 : 0;
     m->group = qe_group_supported(&m->ex);
+    const char *fz = getenv("QE_DECODE_FUSED");
+    m->fused = fz && !strcmp(fz, "1");
     m->tc = qe_tc_supported(&m->ex);
     m->decode = qe_decode_supported(&m->ex);
     if (m->tc) {
@@ -500,6 +506,20 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     const QeMoeConfig &c = m->cfg;
     const int dev = m->device;
     prof_mark(dev, s);
+    const bool decode = m->decode && (m->path == 3 || (m->path == 0 && T <= kDecodeMaxTokens));
+    if (decode && m->fused && c.router_mode == QE_ROUTER_F32) {
+        /* the whole step as one cooperative launch (router, top-k, gate/up, down + combine); its time is
+         * recorded as the router stage, the other stages are empty */
+        const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
+        const int r = qe_launch_decode_fused(&m->ex, m->router_w, m->router_bias, x, T, sc.logits, sc.idx, sc.score,
+                                             sc.h3, I, out, sc.gbar, sms, s);
+        if (r < 0) return -1;
+        if (r == 0) {
+            for (int i = 0; i < 6; i++) prof_mark(dev, s);
+            g_launches += 1;
+            return 0;
+        }
+    }
     if (c.router_mode == QE_ROUTER_F32) {
         if (qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, sc.rpart, s)) return -1;
         g_launches += 1;
@@ -512,7 +532,7 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     g_launches += 1;
     prof_mark(dev, s);
     const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
-    if (m->decode && (m->path == 3 || (m->path == 0 && T <= kDecodeMaxTokens))) {
+    if (decode) {
         /* decode: CUDA-core GEMVs over each selected expert's codes, combine fused into the down projection */
         prof_mark(dev, s);   /* no bucketing */
         if (qe_launch_decode_gateup(&m->ex, x, sc.idx, T, sc.h3, I, s)) return -1;
@@ -1311,7 +1331,10 @@ int qe_profile_end(int device, double *stage_ms, int *passes) {
 
 unsigned long long qe_kernel_launches(void) { return g_launches.load(); }
 
-int qe_device_error(void) { return qe_tc_error(); }
+int qe_device_error(void) {
+    const int t = qe_tc_error(), d = qe_decode_error();
+    return t ? t : d ? 100 + d : 0;
+}
 
 double qe_expert_gb_read(void) { return (double)g_bytes_read.load() / 1e9; }
 double qe_expert_read_seconds(void) { return g_gpu_seconds; }

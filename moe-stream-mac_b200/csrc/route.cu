@@ -152,6 +152,146 @@ __global__ void __launch_bounds__(128) router_gemm_f32_kernel(const float *__res
     }
 }
 
+/* Prefill, register-tiled: CTA = (64 router rows, 64 tokens[, kCG2 chunks of 64 inputs]), 64 threads, each
+ * thread 8 rows (ty + 8i) x 8 tokens (tx + 8j). The W and x tiles of a chunk come by 16-byte cp.async into
+ * shared memory as they lie in HBM ([row][k], [token][k], rows padded to kLds floats: the 4 rows and 8 tokens
+ * a warp reads at one k quad fall in distinct banks), double-buffered. Per chunk every (row, token) value is
+ * one fmaf chain in ascending k (or_dot_f32's order). kSplit (batches with few token tiles): the CTA takes
+ * kCG2 chunks (grid z) and stores each chunk's value to part[chunk][row][token], router_sum2_kernel adds the
+ * chunks in order; otherwise the CTA takes every chunk and adds them in order itself (no partial buffer).
+ * Per k quad a thread loads 8 + 8 float4 for 256 FMAs (128 paired). */
+constexpr int kGR2 = 64, kGT2 = 64, kCG2 = 2, kLds = kChunk + 4, kG2Threads = 64;
+
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+
+template <bool kSplit>
+__global__ void __launch_bounds__(kG2Threads) router_gemm2_f32_kernel(const float *__restrict__ W,
+                                                                      const float *__restrict__ bias,
+                                                                      const float *__restrict__ x, int T, int H,
+                                                                      int E, float *__restrict__ part,
+                                                                      float *__restrict__ logits) {
+    extern __shared__ __align__(16) float sm2[];
+    float *Ws = sm2;                          /* [2][kGR2][kLds] */
+    float *Xs = sm2 + 2 * kGR2 * kLds;        /* [2][kGT2][kLds] */
+    const int tid = threadIdx.x, tx = tid & 7, ty = tid >> 3;
+    const int r0 = blockIdx.x * kGR2, t0 = blockIdx.y * kGT2;
+    const int Ep1 = E + 1;
+    const int nch_all = (H + kChunk - 1) / kChunk;
+    const int cbeg = kSplit ? blockIdx.z * kCG2 : 0, cend = kSplit ? min(nch_all, cbeg + kCG2) : nch_all;
+    float2 total[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int p2 = 0; p2 < 4; p2++) total[i][p2] = make_float2(0.0f, 0.0f);
+    auto load = [&](int c, int b) {
+        const int k0 = c * kChunk;
+#pragma unroll
+        for (int i = 0; i < kGR2 * kChunk / 4 / kG2Threads; i++) {
+            const int idx = tid + kG2Threads * i, row = idx >> 4, q = idx & 15, k = k0 + 4 * q;
+            const bool ok = r0 + row < Ep1 && k + 4 <= H;
+            cp_async16_zfill((uint32_t)__cvta_generic_to_shared(Ws + (b * kGR2 + row) * kLds + 4 * q),
+                             ok ? (const void *)(W + (size_t)(r0 + row) * H + k) : (const void *)W, ok ? 16u : 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < kGT2 * kChunk / 4 / kG2Threads; i++) {
+            const int idx = tid + kG2Threads * i, tok = idx >> 4, q = idx & 15, k = k0 + 4 * q;
+            const bool ok = t0 + tok < T && k + 4 <= H;
+            cp_async16_zfill((uint32_t)__cvta_generic_to_shared(Xs + (b * kGT2 + tok) * kLds + 4 * q),
+                             ok ? (const void *)(x + (size_t)(t0 + tok) * H + k) : (const void *)x, ok ? 16u : 0u);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    load(cbeg, 0);
+    for (int c = cbeg; c < cend; c++) {
+        const int b = (c - cbeg) & 1;
+        if (c + 1 < cend) {
+            load(c + 1, b ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const int kn = min(kChunk, H - c * kChunk);
+        const float *wb = Ws + (b * kGR2 + ty) * kLds, *xb = Xs + (b * kGT2 + tx) * kLds;
+        float2 acc[8][4];   /* [row i][token pair p]: tokens tx + 8*(2p), tx + 8*(2p+1); one fmaf chain each */
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int p2 = 0; p2 < 4; p2++) acc[i][p2] = make_float2(0.0f, 0.0f);
+        for (int kq = 0; kq < kn; kq += 4) {
+            float4 xv[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) xv[j] = *reinterpret_cast<const float4 *>(xb + 8 * j * kLds + kq);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float4 wv = *reinterpret_cast<const float4 *>(wb + 8 * i * kLds + kq);
+                const float w[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const float2 w2 = make_float2(w[kk], w[kk]);
+#pragma unroll
+                    for (int p2 = 0; p2 < 4; p2++) {
+                        const float4 &a = xv[2 * p2], &bq = xv[2 * p2 + 1];
+                        const float xa = kk == 0 ? a.x : kk == 1 ? a.y : kk == 2 ? a.z : a.w;
+                        const float xb2 = kk == 0 ? bq.x : kk == 1 ? bq.y : kk == 2 ? bq.z : bq.w;
+                        acc[i][p2] = __ffma2_rn(w2, make_float2(xa, xb2), acc[i][p2]);
+                    }
+                }
+            }
+        }
+        if constexpr (kSplit) {   /* part[c][row][token] */
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int r = r0 + ty + 8 * i;
+                if (r >= Ep1) continue;
+                float *dst = part + ((size_t)c * Ep1 + r) * T;
+#pragma unroll
+                for (int p2 = 0; p2 < 4; p2++) {
+                    const int ta = t0 + tx + 8 * (2 * p2), tb = ta + 8;
+                    if (ta < T) dst[ta] = acc[i][p2].x;
+                    if (tb < T) dst[tb] = acc[i][p2].y;
+                }
+            }
+        } else {                  /* chunks added in order */
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int p2 = 0; p2 < 4; p2++) total[i][p2] = __fadd2_rn(total[i][p2], acc[i][p2]);
+        }
+        __syncthreads();   /* buffer b is refilled two chunks later */
+    }
+    if constexpr (!kSplit) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = r0 + ty + 8 * i;
+            if (r >= Ep1) continue;
+            const float bv = bias && r < E ? bias[r] : 0.0f;
+#pragma unroll
+            for (int p2 = 0; p2 < 4; p2++) {
+                const int ta = t0 + tx + 8 * (2 * p2), tb = ta + 8;
+                if (ta < T) logits[(size_t)ta * Ep1 + r] = bias && r < E ? __fadd_rn(total[i][p2].x, bv) : total[i][p2].x;
+                if (tb < T) logits[(size_t)tb * Ep1 + r] = bias && r < E ? __fadd_rn(total[i][p2].y, bv) : total[i][p2].y;
+            }
+        }
+    }
+}
+
+/* logits[t][r] = (((0 + part[0][r][t]) + part[1][r][t]) + ...) + bias[r]: or_dot_f32's chunk order; one
+ * thread per (r, t), consecutive threads consecutive tokens (coalesced reads of part). */
+__global__ void router_sum2_kernel(const float *__restrict__ part, const float *__restrict__ bias, int nch, int T,
+                                   int E, float *__restrict__ logits) {
+    const int Ep1 = E + 1;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)T * Ep1) return;
+    const int t = (int)(i % T), r = (int)(i / T);
+    float tot = 0.0f;
+    for (int c = 0; c < nch; c++) tot = __fadd_rn(tot, part[((size_t)c * Ep1 + r) * T + t]);
+    if (bias && r < E) tot = __fadd_rn(tot, bias[r]);
+    logits[(size_t)t * Ep1 + r] = tot;
+}
+
 /* logits[t][r] = (((0 + part[0][t][r]) + part[1][t][r]) + ...) + bias[r]: or_dot_f32's chunk order. */
 __global__ void router_sum_kernel(const float *__restrict__ part, const float *__restrict__ bias, int nch, int T,
                                   int E, float *__restrict__ logits) {
@@ -231,7 +371,24 @@ int qe_launch_router_f32(const float *W, const float *bias, const float *x, int 
     } else {
         if (H % 4) QE_FAIL("router: hidden %d must be a multiple of 4", H);
         const int nch = (H + kChunk - 1) / kChunk;
-        if (part) {
+        const int tiles = ((E + 1 + kGR2 - 1) / kGR2) * ((T + kGT2 - 1) / kGT2);
+        const size_t smem = sizeof(float) * 2 * (kGR2 + kGT2) * kLds;
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (((uintptr_t)W | (uintptr_t)x) % 16 == 0 && tiles >= 2 * sms) {
+            /* enough tiles without splitting the inputs: every CTA adds its chunks itself */
+            dim3 grid((E + 1 + kGR2 - 1) / kGR2, (T + kGT2 - 1) / kGT2);
+            QE_CHECK(qe_set_smem((const void *)router_gemm2_f32_kernel<false>, smem));
+            router_gemm2_f32_kernel<false><<<grid, kG2Threads, smem, s>>>(W, bias, x, T, H, E, nullptr, logits);
+        } else if (part && ((uintptr_t)W | (uintptr_t)x) % 16 == 0) {
+            dim3 grid((E + 1 + kGR2 - 1) / kGR2, (T + kGT2 - 1) / kGT2, (nch + kCG2 - 1) / kCG2);
+            QE_CHECK(qe_set_smem((const void *)router_gemm2_f32_kernel<true>, smem));
+            router_gemm2_f32_kernel<true><<<grid, kG2Threads, smem, s>>>(W, bias, x, T, H, E, part, nullptr);
+            QE_CHECK(cudaGetLastError());
+            const long long n = (long long)T * (E + 1);
+            router_sum2_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, bias, nch, T, E, logits);
+        } else if (part) {
             dim3 grid((E + 1 + kGR - 1) / kGR, (T + kGT - 1) / kGT, (nch + kCG - 1) / kCG);
             router_gemm_f32_kernel<true><<<grid, 128, 0, s>>>(W, bias, x, T, H, E, logits, part);
             QE_CHECK(cudaGetLastError());

@@ -144,25 +144,33 @@ def run_reference_arm(args, cfg):
         return
     threads = os.cpu_count() or 1
     res = time_reference(cfg, 1, args.ref_tokens, args.steps, min(args.warmup, 3), threads, budget_s=150)
+    if res is not None and args.stack:   # one block timed; a token through the stack takes `blocks` passes
+        res["value"] /= cfg.blocks
+        res["sample"] += f"; one block timed, value divided by the stack's {cfg.blocks} blocks"
     if res is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libqref.so (reference build) is missing"}))
         return
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.ref_tokens / res["value"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": workload_config(cfg, world), "cpu_baseline": res,
+            "config": workload_config(cfg, world, cfg.blocks if args.stack else 4, stack=args.stack),
+            "cpu_baseline": res,
             "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
 
 
-def workload_config(cfg, world, blocks=4, ep_mode="rows and partial sums stored into peer memory by the kernels"):
+def workload_config(cfg, world, blocks=4, ep_mode="rows and partial sums stored into peer memory by the kernels",
+                    stack=False):
     mb = blocks * (cfg.E // world * cfg.expert_bytes + cfg.shared_bytes + 4 * cfg.E * cfg.hidden) / 1e6
+    l2 = (f"the whole stack of {blocks} independent blocks runs every step, each fed the step's tokens ({mb:.0f} "
+          f"MB of weights per GPU > 126 MB L2)" if stack else
+          f"{blocks} blocks with distinct weights rotated per step ({mb:.0f} MB of weights per GPU > 126 MB L2)")
     return {"workload": f"{cfg.name}: {cfg.note}", "tokens_per_step": cfg.tokens, "hidden": cfg.hidden,
             "experts": cfg.E, "top_k": cfg.top_k, "inter": cfg.inter, "sh_inter": cfg.sh_inter, "bits": cfg.bits,
             "group_size": cfg.group_size, "router": "fp32", "parallelism": "1 GPU" if world == 1 else
             f"expert parallel over {world} GPUs ({cfg.E // world} experts each; router and shared expert "
             f"replicated; {cfg.tokens} tokens per GPU; exchange: {ep_mode})",
-            "l2": f"{blocks} blocks with distinct weights rotated per step ({mb:.0f} MB of weights per GPU > 126 MB L2)"}
+            "l2": l2, "stack_blocks": blocks if stack else None}
 
 
 def profiled_traffic(kernel: str, config: str):
@@ -276,6 +284,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2")
     ap.add_argument("--blocks", type=int, default=4)
+    ap.add_argument("--stack", action="store_true",
+                    help="one step = one forward of every block of the configuration's stack (c4: 40, c5: 48 "
+                         "independent blocks, each fed the step's tokens); value = tokens through the stack per s")
     ap.add_argument("--ref-tokens", type=int, default=16)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -301,6 +312,8 @@ def main():
                                              device_id=torch.device("cuda", local))
     T = cfg.tokens
     ep = world > 1
+    if args.stack:
+        args.blocks = cfg.blocks
     gen = torch.Generator(device="cuda").manual_seed(7 + rank)
     x = torch.randn(T, cfg.hidden, device="cuda", generator=gen, dtype=torch.float32)
     out = torch.empty_like(x)
@@ -317,13 +330,21 @@ def main():
         blocks = [m.engine.block for m in models]
 
         def step(i):
-            models[i % len(models)].forward(x, mode=args.ep_mode)
+            if args.stack:
+                for mdl in models:
+                    mdl.forward(x, mode=args.ep_mode)
+            else:
+                models[i % len(models)].forward(x, mode=args.ep_mode)
     else:
         blocks = [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size,
                                 max_tokens=T, device=local, seed=b + 1, block=b) for b in range(args.blocks)]
 
         def step(i):
-            blocks[i % len(blocks)].forward_device(T, x.data_ptr(), out.data_ptr(), sptr)
+            if args.stack:
+                for b in blocks:
+                    b.forward_device(T, x.data_ptr(), out.data_ptr(), sptr)
+            else:
+                blocks[i % len(blocks)].forward_device(T, x.data_ptr(), out.data_ptr(), sptr)
 
         use_graph = args.graph == "on" or (args.graph == "auto" and T <= 4)
         if use_graph:   # one captured forward per block, replayed (no per-kernel host launch cost)
@@ -331,7 +352,11 @@ def main():
             eager_step = step
 
             def step(i):
-                graphs[i % len(graphs)].launch(sptr)
+                if args.stack:
+                    for g in graphs:
+                        g.launch(sptr)
+                else:
+                    graphs[i % len(graphs)].launch(sptr)
 
     def barrier():
         if world > 1:
@@ -374,15 +399,17 @@ def main():
     xh = torch.randn(T, cfg.hidden, generator=torch.Generator().manual_seed(11 + rank)).pin_memory()
     oh = torch.empty_like(xh).pin_memory()
     xn, on = xh.numpy(), oh.numpy()
-    ke = max(10, min(args.steps, 200))
+    ke = max(10, min(args.steps, 200)) if not args.stack else 5
 
     def e2e_step(i):
-        if ep:   # qmoe.ep.ExpertParallelMoe.forward with the copies in and out of pinned host memory
-            xd = xh.to("cuda", non_blocking=True)
-            oh.copy_(models[i % len(models)].forward(xd, mode=args.ep_mode), non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-        else:    # qe_moe_forward: host buffers in and out
-            blocks[i % len(blocks)].forward(xn, on)
+        sel = range(len(blocks)) if args.stack else [i % len(blocks)]
+        for bi in sel:
+            if ep:   # qmoe.ep.ExpertParallelMoe.forward with the copies in and out of pinned host memory
+                xd = xh.to("cuda", non_blocking=True)
+                oh.copy_(models[bi].forward(xd, mode=args.ep_mode), non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+            else:    # qe_moe_forward: host buffers in and out
+                blocks[bi].forward(xn, on)
 
     for i in range(3):
         e2e_step(i)
@@ -434,13 +461,19 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": dict(workload_config(cfg, world, args.blocks, "rows and partial sums stored into peer memory by "
-                                           "the kernels" if args.ep_mode == "p2p" else "all_to_all over NCCL"),
+                                           "the kernels" if args.ep_mode == "p2p" else "all_to_all over NCCL",
+                                           args.stack),
                            cuda_graph=use_graph),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * cfg.hidden,
                     "d2h_bytes_per_step": 4 * T * cfg.hidden, "steps": ke, "timing": "host clock, max over ranks"},
             "roofline": roofline, "gpu_launches": launches, "clocks": clk}
+    if args.stack:   # every token passes through all blocks of the stack: block-level throughput for reference
+        line["block_tokens_per_s"] = value * args.blocks
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = time_reference(cfg, 1, args.ref_tokens, 1000, 1, os.cpu_count() or 1, budget_s=args.cpu_budget)
+        if cb and args.stack:   # one block timed; a token through the stack takes `blocks` such passes
+            cb["value"] /= args.blocks
+            cb["sample"] += f"; one block timed, value divided by the stack's {args.blocks} blocks"
         line["cpu_baseline"] = cb if cb else {"value": None, "unavailable": "oracle/_ref missing"}
     if ep:
         for mdl in models:

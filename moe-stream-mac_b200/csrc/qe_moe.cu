@@ -940,8 +940,11 @@ int qe_moe_forward(QeMoe *m, int T, const float *x, float *out) {
         QE_CHECK(cudaMemcpyAsync(sc.x, x + (size_t)t0 * H, sizeof(float) * n * H, cudaMemcpyHostToDevice, s));
         if (run_pass(m, sc.x, sc.out, n, sc, d->sms, s)) return -1;
         QE_CHECK(cudaMemcpyAsync(out + (size_t)t0 * H, sc.out, sizeof(float) * n * H, cudaMemcpyDeviceToHost, s));
-        int32_t na = 0;
-        QE_CHECK(cudaMemcpyAsync(&na, sc.b.n_active, 4, cudaMemcpyDeviceToHost, s));
+        /* experts read by this pass: the active buckets (bucketed paths), or every selected slot plus the
+         * shared expert (decode path, no buckets: an upper bound when tokens share experts) */
+        const bool decode = m->decode && (m->path == 3 || (m->path == 0 && n <= kDecodeMaxTokens));
+        int32_t na = n * m->cfg.top_k + 1;
+        if (!decode) QE_CHECK(cudaMemcpyAsync(&na, sc.b.n_active, 4, cudaMemcpyDeviceToHost, s));
         if (tracing) {
             idx_host.resize((size_t)n * m->cfg.top_k);
             QE_CHECK(cudaMemcpyAsync(idx_host.data(), sc.idx, 4 * idx_host.size(), cudaMemcpyDeviceToHost, s));

@@ -146,25 +146,23 @@ __device__ __noinline__ void route_token_sequential(const float *lg, int E, int 
         for (int i = 0; i < E; i++) probs_out[i] = probs_s[i];
 }
 
-/* Token t (one warp): lg = its logits, probs_s/idx_s = 2*E floats of this warp's shared memory; writes
- * idx_out[t*k ..], score_out[t*k ..] and, when probs_out is given, probs_out[t*E ..]. */
-__device__ __forceinline__ void route_topk_warp(const float *__restrict__ lg, int t, int E, int k, float *probs_s,
-                                                int *idx_s, int32_t *__restrict__ idx_out,
-                                                float *__restrict__ score_out, float *__restrict__ probs_out) {
+template <int EPL>
+__device__ __forceinline__ void route_topk_warp_t(const float *__restrict__ lg, int t, int E, int k, float *probs_s,
+                                                  int *idx_s, int32_t *__restrict__ idx_out,
+                                                  float *__restrict__ score_out, float *__restrict__ probs_out) {
+    /* lane holds experts lane + 32*i, i < EPL; slots past E hold -inf (exp 0, never selected before a valid
+     * expert: equal values keep the lower index). The per-slot loops carry no conditions, so the lane's
+     * exponentials and divisions run as independent chains. */
     const int lane = threadIdx.x & 31;
-    const int epl = (E + 31) / 32;
-
-    float v[kMaxEPL];
+    float v[EPL];
     bool has_nan = false;
     float mx = -__int_as_float(0x7f800000);
 #pragma unroll
-    for (int i = 0; i < kMaxEPL; i++) {
+    for (int i = 0; i < EPL; i++) {
         const int e = lane + 32 * i;
-        v[i] = (i < epl && e < E) ? lg[e] : 0.0f;
-        if (i < epl && e < E) {
-            has_nan |= (v[i] != v[i]);
-            mx = fmaxf(mx, v[i]);
-        }
+        v[i] = e < E ? lg[e] : -__int_as_float(0x7f800000);
+        has_nan |= (v[i] != v[i]);
+        mx = fmaxf(mx, v[i]);
     }
     has_nan = __any_sync(QE_FULL, has_nan);
     if (has_nan) {
@@ -176,15 +174,11 @@ __device__ __forceinline__ void route_topk_warp(const float *__restrict__ lg, in
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(QE_FULL, mx, o));
 
-    double part = 0.0;
 #pragma unroll
-    for (int i = 0; i < kMaxEPL; i++) {
-        const int e = lane + 32 * i;
-        if (i < epl && e < E) {
-            v[i] = qe_expf(__fsub_rn(v[i], mx));
-            part = __dadd_rn(part, (double)v[i]);
-        }
-    }
+    for (int i = 0; i < EPL; i++) v[i] = qe_expf(__fsub_rn(v[i], mx));
+    double part = 0.0;   /* slots past E add +0.0: no change */
+#pragma unroll
+    for (int i = 0; i < EPL; i++) part = __dadd_rn(part, (double)v[i]);
 #pragma unroll
     for (int o = 16; o; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(QE_FULL, part, o));
     float sf = __double2float_rn(part);
@@ -195,9 +189,9 @@ __device__ __forceinline__ void route_topk_warp(const float *__restrict__ lg, in
         const bool safe = (part - B > mid_lo) && (part + B < mid_hi);
         if (!safe) { /* uniform across the warp: every lane holds the same part */
 #pragma unroll
-            for (int i = 0; i < kMaxEPL; i++) {
+            for (int i = 0; i < EPL; i++) {
                 const int e = lane + 32 * i;
-                if (i < epl && e < E) probs_s[e] = v[i];
+                if (e < E) probs_s[e] = v[i];
             }
             __syncwarp();
             double seq = 0.0;
@@ -210,10 +204,11 @@ __device__ __forceinline__ void route_topk_warp(const float *__restrict__ lg, in
     }
     unsigned used = 0;
 #pragma unroll
-    for (int i = 0; i < kMaxEPL; i++) {
+    for (int i = 0; i < EPL; i++) v[i] = __fdiv_rn(v[i], sf);
+#pragma unroll
+    for (int i = 0; i < EPL; i++) {
         const int e = lane + 32 * i;
-        if (i < epl && e < E) {
-            v[i] = __fdiv_rn(v[i], sf);
+        if (e < E) {
             if (probs_out) probs_out[(size_t)t * E + e] = v[i];
         } else {
             used |= 1u << i; /* not a candidate */
@@ -225,7 +220,7 @@ __device__ __forceinline__ void route_topk_warp(const float *__restrict__ lg, in
         float bv = -__int_as_float(0x7f800000);
         int bi = 0x7fffffff, bslot = -1;
 #pragma unroll
-        for (int i = 0; i < kMaxEPL; i++) {
+        for (int i = 0; i < EPL; i++) {
             if (!(used >> i & 1u) && (bslot < 0 || v[i] > bv)) { /* ascending i = ascending index */
                 bv = v[i];
                 bi = lane + 32 * i;
@@ -252,6 +247,19 @@ __device__ __forceinline__ void route_topk_warp(const float *__restrict__ lg, in
         idx_out[(size_t)t * k + lane] = isel;
         score_out[(size_t)t * k + lane] = __fdiv_rn(psel, ssum);
     }
+}
+
+/* Token t (one warp): lg = its logits, probs_s/idx_s = 2*E floats of this warp's shared memory; writes
+ * idx_out[t*k ..], score_out[t*k ..] and, when probs_out is given, probs_out[t*E ..]. E <= 32*kMaxEPL. */
+__device__ __forceinline__ void route_topk_warp(const float *__restrict__ lg, int t, int E, int k, float *probs_s,
+                                                int *idx_s, int32_t *__restrict__ idx_out,
+                                                float *__restrict__ score_out, float *__restrict__ probs_out) {
+    const int epl = (E + 31) / 32;
+    if (epl <= 1) route_topk_warp_t<1>(lg, t, E, k, probs_s, idx_s, idx_out, score_out, probs_out);
+    else if (epl <= 2) route_topk_warp_t<2>(lg, t, E, k, probs_s, idx_s, idx_out, score_out, probs_out);
+    else if (epl <= 4) route_topk_warp_t<4>(lg, t, E, k, probs_s, idx_s, idx_out, score_out, probs_out);
+    else if (epl <= 8) route_topk_warp_t<8>(lg, t, E, k, probs_s, idx_s, idx_out, score_out, probs_out);
+    else route_topk_warp_t<16>(lg, t, E, k, probs_s, idx_s, idx_out, score_out, probs_out);
 }
 
 }  // namespace

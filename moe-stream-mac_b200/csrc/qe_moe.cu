@@ -563,14 +563,14 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     }
     const bool use_tc = m->tc && (m->path == 2 || (m->path == 0 && T >= kTcMinTokens));
     if (use_tc) {
-        const int R = qe_tc_bm(), NB = qe_tc_bn();
+        const int R = qe_tc_bm(), NB = qe_tc_tokens_per_tile(T, c.top_k, c.E);
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
                   tiles_dn = (c.hidden + R - 1) / R;
         if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s)) return -1;
         prof_mark(dev, s);
-        if (qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, T, &sc.tcb, sms, s)) return -1;
+        if (qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, T, NB, &sc.tcb, sms, s)) return -1;
         prof_mark(dev, s);
-        if (qe_launch_tc_down(&m->ex, m->maps_dn, &sc.b, T, &sc.tcb, sc.ybuf, sms, s)) return -1;
+        if (qe_launch_tc_down(&m->ex, m->maps_dn, &sc.b, T, NB, &sc.tcb, sc.ybuf, sms, s)) return -1;
         prof_mark(dev, s);
         if (qe_launch_combine(sc.ybuf, sc.score, sc.logits, c.E + 1, T, c.E, c.top_k, c.hidden, out, s)) return -1;
         prof_mark(dev, s);
@@ -728,12 +728,12 @@ int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sm
             return -1;
         g_launches += 3;
     } else if (use_tc) {
-        const int R = qe_tc_bm(), NB = qe_tc_bn();
+        const int R = qe_tc_bm(), NB = qe_tc_tokens_per_tile(n, c.top_k, c.E);
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
                   tiles_dn = (c.hidden + R - 1) / R;
         if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s) ||
-            qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, n, &sc.tcb, sms, s) ||
-            qe_launch_tc_down(&m->ex, m->maps_dn, &sc.b, n, &sc.tcb, sc.ybuf, sms, s))
+            qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, n, NB, &sc.tcb, sms, s) ||
+            qe_launch_tc_down(&m->ex, m->maps_dn, &sc.b, n, NB, &sc.tcb, sc.ybuf, sms, s))
             return -1;
         g_launches += 4;
     } else {

@@ -179,6 +179,7 @@ struct QeMoe {
     bool tc;                /* tensor-core path available for this shape */
     bool decode;            /* decode GEMVs available for this shape */
     bool group;             /* grouped GEMVs available for this shape */
+    int tile;               /* tensor-core token tile: 0 = by load, else 32 or 64 (QE_TC_TILE) */
     bool fused;             /* decode steps as one cooperative launch (QE_DECODE_FUSED=1; measured slower than
                              * the four launches replayed from a CUDA graph, so off by default) */
     alignas(64) unsigned char maps_gu[2 * 2 * 3 * 128];  /* [routed/shared][gate/up][codes, scales, biases] */
@@ -276,6 +277,8 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     m->group = qe_group_supported(&m->ex);
     const char *fz = getenv("QE_DECODE_FUSED");
     m->fused = fz && !strcmp(fz, "1");
+    const char *tt = getenv("QE_TC_TILE");
+    m->tile = tt && !strcmp(tt, "32") ? 32 : tt && !strcmp(tt, "64") ? 64 : 0;
     m->tc = qe_tc_supported(&m->ex);
     m->decode = qe_decode_supported(&m->ex);
     if (m->tc) {
@@ -563,7 +566,7 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     }
     const bool use_tc = m->tc && (m->path == 2 || (m->path == 0 && T >= kTcMinTokens));
     if (use_tc) {
-        const int R = qe_tc_bm(), NB = qe_tc_tokens_per_tile(T, c.top_k, c.E);
+        const int R = qe_tc_bm(), NB = m->tile ? m->tile : qe_tc_tokens_per_tile(T, c.top_k, c.E);
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
                   tiles_dn = (c.hidden + R - 1) / R;
         if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s)) return -1;
@@ -728,7 +731,7 @@ int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sm
             return -1;
         g_launches += 3;
     } else if (use_tc) {
-        const int R = qe_tc_bm(), NB = qe_tc_tokens_per_tile(n, c.top_k, c.E);
+        const int R = qe_tc_bm(), NB = m->tile ? m->tile : qe_tc_tokens_per_tile(n, c.top_k, c.E);
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
                   tiles_dn = (c.hidden + R - 1) / R;
         if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s) ||

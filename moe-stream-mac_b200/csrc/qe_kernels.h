@@ -16,11 +16,17 @@ struct QeQDev {
 };
 
 /* Routing: fp32 router logits for E experts plus one extra column (index E) holding the shared-expert
- * gate logit, logits[T][E+1]. */
+ * gate logit, logits[T][E+1]. qe_launch_router_f32 returns the number of kernels it launched, or -1. */
 int qe_launch_router_f32(const float *W /*[E+1][H]*/, const float *bias /*[E] or null*/, const float *x,
                          int T, int H, int E, float *logits,
                          float *part /* [ceil(H/64)][T][E+1] scratch for the chunk-split prefill GEMM, or null */,
+                         const float *Wd /* [H][qe_router_wd_rows(E)][2] duplicated weights, or null */,
+                         float *xt /* [H][T rounded up to 4] scratch for the transposed batch, or null */,
                          cudaStream_t s);
+/* Rows and contents of the paired-FMA prefill router's weight copy Wd[k][row][2] (rows past E are zero; when
+ * E + 1 = 64n + 1 the gate row E is read from W instead). */
+int qe_router_wd_rows(int E);
+int qe_launch_router_wd_fill(const float *W, int H, int E, float *Wd, cudaStream_t s);
 int qe_launch_router_qmat(const QeQDev *router /*[E][H]*/, const QeQDev *sh_router /*[1][H]*/, const float *x,
                           int T, int H, int E, float *logits, cudaStream_t s);
 int qe_launch_route_topk(const float *logits, int ld, int T, int E, int k, int32_t *idx, float *score,

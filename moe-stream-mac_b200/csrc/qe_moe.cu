@@ -117,6 +117,7 @@ size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 struct Scratch {
     float *x, *out, *logits, *score, *h3, *ybuf;
     float *rpart;               /* fp32 router chunk values [hidden/64][T][E+1] (prefill GEMM) */
+    float *rxt;                 /* the batch transposed for the prefill router GEMM, [hidden][T rounded up to 4] */
     int32_t *idx;
     QeBuckets b;
     QeTcBufs tcb;               /* tensor-core path: split activations, group sums, unscale factors */
@@ -137,6 +138,7 @@ size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
     t.out = (float *)take(sizeof(float) * (size_t)T * c.hidden);
     t.logits = (float *)take(sizeof(float) * (size_t)T * (E + 1));
     t.rpart = (float *)take(sizeof(float) * (size_t)((c.hidden + 63) / 64) * T * (E + 1));
+    t.rxt = (float *)take(sizeof(float) * (size_t)c.hidden * ((T + 3) & ~3));
     t.score = (float *)take(sizeof(float) * (size_t)T * k);
     t.idx = (int32_t *)take(sizeof(int32_t) * (size_t)T * k);
     t.h3 = (float *)take(sizeof(float) * npair * I);
@@ -170,6 +172,7 @@ struct QeMoe {
     void *weights;          /* one HBM allocation holding every tensor of the block */
     size_t weight_bytes;
     float *router_w;        /* [E+1][H] (F32 mode; row E = shared gate) */
+    float *router_wd;       /* [H][qe_router_wd_rows(E)][2]: router_w duplicated for the prefill GEMM (F32 mode) */
     float *router_bias;     /* [E] or null */
     QeQDev router_q, sh_router_q;
     QeExpertArgs ex;
@@ -244,7 +247,9 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
         qbytes(p.n, p.rows, p.cols, p.bits, gs, &wb, &gb);
         total += align256(wb) + 2 * align256(gb);
     }
-    if (c->router_mode == QE_ROUTER_F32) total += align256(sizeof(float) * (size_t)(E + 1) * H) + align256(4 * (size_t)E);
+    const size_t wd_bytes = sizeof(float) * 2 * (size_t)H * qe_router_wd_rows(E);
+    if (c->router_mode == QE_ROUTER_F32)
+        total += align256(sizeof(float) * (size_t)(E + 1) * H) + align256(4 * (size_t)E) + align256(wd_bytes);
     char *base = nullptr;
     if (cudaMalloc((void **)&base, total) != cudaSuccess) {
         fprintf(stderr, "qengine_b200: cannot allocate %zu bytes of HBM for the block\n", total);
@@ -267,6 +272,7 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     if (c->router_mode == QE_ROUTER_F32) {
         m->router_w = (float *)(base + off); off += align256(sizeof(float) * (size_t)(E + 1) * H);
         m->router_bias = (float *)(base + off); off += align256(4 * (size_t)E);
+        m->router_wd = (float *)(base + off); off += align256(wd_bytes);
     }
     m->ex.E = El; m->ex.k = c->top_k; m->ex.hidden = H; m->ex.inter = I; m->ex.sh_inter = Is;
     size_t wb, gb;
@@ -428,6 +434,7 @@ QeMoe *qe_moe_create(const QeMoeConfig *cfg, const QeMoeWeights *w) {
             const size_t H = cfg->hidden, E = cfg->E;
             rc = cudaMemcpyAsync(m->router_w, w->router_f32, 4 * E * H, cudaMemcpyHostToDevice, s) != cudaSuccess ||
                  cudaMemcpyAsync(m->router_w + E * H, w->sh_gate_f32, 4 * H, cudaMemcpyHostToDevice, s) != cudaSuccess;
+            if (!rc) rc = qe_launch_router_wd_fill(m->router_w, (int)H, (int)E, m->router_wd, s);
             if (!rc && w->router_bias)
                 rc = cudaMemcpyAsync(m->router_bias, w->router_bias, 4 * E, cudaMemcpyHostToDevice, s) != cudaSuccess;
             if (!w->router_bias) m->router_bias = nullptr;
@@ -462,7 +469,8 @@ QeMoe *qe_moe_create_synthetic(const QeMoeConfig *cfg, uint64_t seed, uint32_t b
     if (!rc && cfg->router_mode == QE_ROUTER_F32) {
         const float c = syn_sigma_c(0.02);
         rc = qe_launch_synth_normal(seed, block, SYN_ROUTER, (size_t)E * H, c, m->router_w, s) ||
-             qe_launch_synth_normal(seed, block, SYN_SHGATE, (size_t)H, c, m->router_w + (size_t)E * H, s);
+             qe_launch_synth_normal(seed, block, SYN_SHGATE, (size_t)H, c, m->router_w + (size_t)E * H, s) ||
+             qe_launch_router_wd_fill(m->router_w, H, E, m->router_wd, s);
         if (!rc && router_bias)
             rc = cudaMemcpyAsync(m->router_bias, router_bias, 4 * (size_t)E, cudaMemcpyHostToDevice, s) != cudaSuccess;
         if (!router_bias) m->router_bias = nullptr;
@@ -498,11 +506,17 @@ namespace {
 int run_route(QeMoe *m, const float *x, int T, Scratch &sc, cudaStream_t s) {
     const QeMoeConfig &c = m->cfg;
     if (c.router_mode == QE_ROUTER_F32) {
-        if (qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, sc.rpart, s)) return -1;
+        const int nr = qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, sc.rpart,
+                                            m->router_wd, sc.rxt, s);
+        if (nr < 0) return -1;
+        g_launches += nr;
     } else {
         if (qe_launch_router_qmat(&m->router_q, &m->sh_router_q, x, T, c.hidden, c.E, sc.logits, s)) return -1;
+        g_launches += 2;
     }
-    return qe_launch_route_topk(sc.logits, c.E + 1, T, c.E, c.top_k, sc.idx, sc.score, nullptr, s);
+    if (qe_launch_route_topk(sc.logits, c.E + 1, T, c.E, c.top_k, sc.idx, sc.score, nullptr, s)) return -1;
+    g_launches += 1;
+    return 0;
 }
 
 int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, cudaStream_t s) {
@@ -524,8 +538,10 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
         }
     }
     if (c.router_mode == QE_ROUTER_F32) {
-        if (qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, sc.rpart, s)) return -1;
-        g_launches += 1;
+        const int nr = qe_launch_router_f32(m->router_w, m->router_bias, x, T, c.hidden, c.E, sc.logits, sc.rpart,
+                                            m->router_wd, sc.rxt, s);
+        if (nr < 0) return -1;
+        g_launches += nr;
     } else {
         if (qe_launch_router_qmat(&m->router_q, &m->sh_router_q, x, T, c.hidden, c.E, sc.logits, s)) return -1;
         g_launches += 2;
@@ -1005,7 +1021,7 @@ int qe_moe_ep_route_device(QeMoe *m, int T, const float *x, int32_t *meta, float
         QE_CHECK(cudaGetLastError());
         QE_CHECK(cudaMemsetAsync(sc.idx, 0xff, sizeof(int32_t) * (size_t)n * k, s));   /* shared expert only */
         if (run_experts(m, x + (size_t)t0 * H, shared + (size_t)t0 * H, n, sc, d->sms, false, true, s)) return -1;
-        g_launches += 3;
+        g_launches += 1;   /* ep_meta_kernel */
     }
     return 0;
 }

@@ -42,6 +42,8 @@ extern "C" int qe_route_f32_noalloc(const float *router_w, const float *router_b
         g_noalloc_logits[dev] = static_cast<float *>(p);
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (qe_launch_router_f32(router_w, router_bias, x, T, hidden, E, g_noalloc_logits[dev], nullptr, s)) return -1;
+    if (qe_launch_router_f32(router_w, router_bias, x, T, hidden, E, g_noalloc_logits[dev], nullptr, nullptr, nullptr,
+                             s) < 0)
+        return -1;
     return qe_launch_route_topk(g_noalloc_logits[dev], E + 1, T, E, top_k, idx, score, nullptr, s);
 }

@@ -263,10 +263,13 @@ def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, mode, np
     H, I = cfg.hidden, cfg.inter
     # weights of the touched experts once; x rows in, partial rows out; h3 written and read; y per pair
     nbytes = uniq * cfg.expert_bytes + 8 * rows * H + 8 * pairs * I + 4 * pairs * H
-    achieved = nbytes / (phase_ms["experts"] / 1e3) / 1e9
     G, T = world, cfg.tokens
+    if mode == "p2p" and (G + 1) * T <= models[0].engine.block.cfg.max_tokens:
+        # the shared expert on this rank's own T rows runs in the same launches (qe_moe_ep_route_p2p)
+        nbytes += cfg.shared_bytes + 8 * T * H + 8 * T * cfg.sh_inter + 4 * T * H
+    achieved = nbytes / (phase_ms["experts"] / 1e3) / 1e9
     xbytes = (G - 1) * T * (4 * H + 8 * cfg.top_k)   # rows + slot lists sent to the other ranks (padded blocks)
-    return {"bound": "hbm", "kernel": f"expert stage (qe_moe_ep_experts_device) on rank {rank}", "achieved": achieved,
+    return {"bound": "hbm", "kernel": f"expert stage (qe_moe_ep_experts_{'p2p' if mode == 'p2p' else 'device'}) on rank {rank}", "achieved": achieved,
             "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None, "peak_source": peak_source,
             "algorithmic_bytes_per_launch": nbytes, "unique_local_experts": uniq,
             "phase_ms": {k: round(v, 5) for k, v in phase_ms.items()},
@@ -322,7 +325,7 @@ def main():
     use_graph = False
     if ep:
         from qmoe.ep import ExpertParallelMoe
-        models = [ExpertParallelMoe.on_gpu(cfg, rank, world, local, seed=b + 1, block=b, max_tokens=world * T)
+        models = [ExpertParallelMoe.on_gpu(cfg, rank, world, local, seed=b + 1, block=b, max_tokens=(world + 1) * T)
                   for b in range(args.blocks)]
         if args.ep_mode == "p2p":
             for mdl in models:

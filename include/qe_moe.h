@@ -151,7 +151,13 @@ int qe_moe_ep_size(const QeMoe *m);
  *                            home rank's return buffer
  *   (caller) a barrier across the ranks on the stream
  *   qe_moe_ep_combine_p2p    out[t] = sum over ranks d ascending of return[d][home[d][t]] + shared[t]
- * Same arithmetic as the all_to_all step (bit-identical results). No multicast, only plain loads and stores. */
+ * Same arithmetic as the all_to_all step (bit-identical results). No multicast, only plain loads and stores.
+ * Folded shared expert: routing the step with qe_moe_ep_route_p2p instead of qe_moe_ep_route_device computes
+ * no shared term there; it copies the rank's own rows and shared-gate logits into the exchange, the expert
+ * stage then runs the shared expert on them in the same launches as the received rows, and
+ * qe_moe_ep_combine_p2p is called with shared = NULL (the term is read from the exchange). Same arithmetic
+ * per token; the shared expert's batch is then the expert stage's, not the T own rows. Needs
+ * T <= T_max and T <= the handle's max_tokens (and (G+1)*T <= max_tokens for one expert-stage pass). */
 typedef struct QeEpXchg QeEpXchg;
 QeEpXchg *qe_ep_xchg_create(QeMoe *m, int T_max, void *handle);
 int qe_ep_xchg_handle_bytes(void);
@@ -160,6 +166,7 @@ int qe_ep_xchg_connect_local(QeEpXchg *const *all, int n);
 void qe_ep_xchg_free(QeEpXchg *x);
 int qe_moe_ep_dispatch_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, const int32_t *meta, int32_t *home,
                            int32_t *counts, void *stream);
+int qe_moe_ep_route_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, int32_t *meta, void *stream);
 int qe_moe_ep_experts_p2p(QeMoe *m, QeEpXchg *xc, int T, void *stream);
 int qe_moe_ep_combine_p2p(QeMoe *m, QeEpXchg *xc, int T, const int32_t *home, const float *shared, float *out,
                           void *stream);

@@ -40,8 +40,8 @@ __device__ int warp_exclusive_scan(int *a, int n, int lane) {
 __device__ __forceinline__ int *cnt_tmp(int *sm, int E) { return sm + 6 * (E + 2); }
 
 __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restrict__ idx, int T, int E, int k,
-                                                          int shared_tokens, int tiles_gu, int tiles_sh_gu,
-                                                          int tiles_dn, int chunk, QeBuckets b) {
+                                                          int shared_tokens, int shared_first, int tiles_gu,
+                                                          int tiles_sh_gu, int tiles_dn, int chunk, QeBuckets b) {
     extern __shared__ int sm[];
     int *cnt = sm;                 /* [E+1] */
     int *off = cnt + (E + 1);      /* [E+2] */
@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restr
         if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    if (tid == 0) cnt[E] = shared_tokens;   /* T, or 0 when the shared expert is computed elsewhere */
+    if (tid == 0) cnt[E] = shared_tokens;   /* rows shared_first.. of the batch, or 0 (computed elsewhere) */
     __syncthreads();
     for (int e = tid; e <= E; e += kThreads) {
         off[e] = cnt[e];
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restr
         const int pos = atomicAdd(&cur[e], 1);
         b.pairs[pos] = t * (k + 1) + j;
     }
-    for (int t = tid; t < shared_tokens; t += kThreads) b.pairs[off[E] + t] = t * (k + 1) + k;
+    for (int t = tid; t < shared_tokens; t += kThreads) b.pairs[off[E] + t] = (shared_first + t) * (k + 1) + k;
     for (int e = tid; e <= E; e += kThreads) {
         b.counts[e] = cnt[e];
         b.offsets[e] = off[e];
@@ -128,9 +128,12 @@ __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restr
 }  // namespace
 
 int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int shared_tokens, int tiles_gu, int tiles_sh_gu,
-                     int tiles_dn, int chunk, const QeBuckets *b, cudaStream_t s) {
+                     int tiles_dn, int chunk, const QeBuckets *b, cudaStream_t s, int shared_first) {
+    if (shared_first < 0 || shared_tokens < 0 || shared_first + shared_tokens > T)
+        QE_FAIL("bucket: shared rows [%d, %d) outside the batch of %d", shared_first, shared_first + shared_tokens, T);
     const size_t smem = sizeof(int) * (size_t)(8 * (E + 2));
-    bucket_kernel<<<1, kThreads, smem, s>>>(idx, T, E, k, shared_tokens, tiles_gu, tiles_sh_gu, tiles_dn, chunk, *b);
+    bucket_kernel<<<1, kThreads, smem, s>>>(idx, T, E, k, shared_tokens, shared_first, tiles_gu, tiles_sh_gu, tiles_dn,
+                                            chunk, *b);
     QE_CHECK(cudaGetLastError());
     return 0;
 }

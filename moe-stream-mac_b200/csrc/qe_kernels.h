@@ -42,8 +42,9 @@ struct QeBuckets {
     int32_t *slot_items;  /* [2][E+2] per-slot work-item prefix, gate/up & down */
     int32_t *n_active;    /* [3]: active slots, gate/up items, down items     */
 };
+/* The shared expert's bucket holds rows [shared_first, shared_first + shared_tokens) of the batch. */
 int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int shared_tokens, int tiles_gu, int tiles_sh_gu,
-                     int tiles_dn, int chunk, const QeBuckets *b, cudaStream_t s);
+                     int tiles_dn, int chunk, const QeBuckets *b, cudaStream_t s, int shared_first = 0);
 
 /* Expert kernels (mma.sync split-bf16 path). */
 struct QeExpertArgs {

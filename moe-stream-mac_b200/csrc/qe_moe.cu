@@ -619,6 +619,12 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
 
 /* ------------------------------------------------------------------ expert parallelism */
 
+/* gate[t] = the shared-expert gate logit of token t (router column E). */
+__global__ void ep_gate_kernel(const float *__restrict__ logits, int T, int E, float *__restrict__ gate) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < T) gate[t] = logits[(size_t)t * (E + 1) + E];
+}
+
 /* meta[T][2k]: the routing result per token, global expert ids then the scores' bits */
 __global__ void ep_meta_kernel(const int32_t *__restrict__ idx, const float *__restrict__ score, int T, int k,
                                int32_t *__restrict__ meta) {
@@ -726,22 +732,30 @@ struct EpScatter {
     int row0, Tblk, self;
 };
 
+/* The rank's own tokens appended to the received rows (rows sh0 .. sh0 + sh_n - 1 of the pass, no routed slot):
+ * the shared expert runs on them in the same launches, and sigmoid(gate[i]) * y_shared goes to sh_out[i]. */
+struct EpFold {
+    int sh0, sh_n;
+    const float *gate;
+    float *sh_out;
+};
+
 /* The expert stages for n rows whose local slot ids and scores are in sc.idx / sc.score (and, for the shared
  * expert, whose gate logits are in sc.logits): bucket, gate/up + SwiGLU, down, then the selective combine
  * into out[n][hidden], or (scatter) into the home ranks' return buffers. */
 int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sms, bool routed, bool shared,
-                cudaStream_t s, const EpScatter *scatter = nullptr) {
+                cudaStream_t s, const EpScatter *scatter = nullptr, const EpFold *fold = nullptr) {
     const QeMoeConfig &c = m->cfg;
     const int El = m->E_loc, k = c.top_k;
     const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
-    const int sh_tokens = shared ? n : 0;
+    const int sh_tokens = fold ? fold->sh_n : shared ? n : 0, sh0 = fold ? fold->sh0 : 0;
     const bool use_group = m->group && m->path == 4;
     const bool use_tc = !use_group && m->tc && (m->path == 2 || (m->path == 0 && n >= kTcMinTokens));
     if (use_group) {
         const int R = qe_group_rows(), NB = qe_group_tokens();
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
                   tiles_dn = (c.hidden + R - 1) / R;
-        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s) ||
+        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s, sh0) ||
             qe_launch_group_gateup(&m->ex, x, &sc.b, sms, sc.h3, I, s) ||
             qe_launch_group_down(&m->ex, sc.h3, I, &sc.b, sms, sc.ybuf, s))
             return -1;
@@ -750,7 +764,7 @@ int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sm
         const int R = qe_tc_bm(), NB = m->tile ? m->tile : qe_tc_tokens_per_tile(n, c.top_k, c.E);
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
                   tiles_dn = (c.hidden + R - 1) / R;
-        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s) ||
+        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s, sh0) ||
             qe_launch_tc_gateup(&m->ex, m->maps_gu, x, &sc.b, n, NB, &sc.tcb, sms, s) ||
             qe_launch_tc_down(&m->ex, m->maps_dn, &sc.b, n, NB, &sc.tcb, sc.ybuf, sms, s))
             return -1;
@@ -765,11 +779,25 @@ int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sm
         const int tmax = std::max(tiles_gu, tiles_sh);
         const int grid_gu = (int)std::min<long long>(chunks * tmax, 16LL * sms);
         const int grid_dn = (int)std::min<long long>(chunks * tiles_dn, 16LL * sms);
-        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, chunk, &sc.b, s) ||
+        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, chunk, &sc.b, s, sh0) ||
             qe_launch_gateup(&m->ex, x, &sc.b, n, sc.h3, I, grid_gu, s) ||
             qe_launch_down(&m->ex, sc.h3, I, &sc.b, n, sc.ybuf, grid_dn, s))
             return -1;
         g_launches += 3;
+    }
+    if (fold) {
+        /* received rows [0, sh0): partial sums into the home ranks; own rows: the gated shared expert */
+        const size_t H = c.hidden;
+        if (sh0 > 0 && qe_launch_combine_sel_scatter(sc.ybuf, sc.idx, sc.score, sh0, k, c.hidden, scatter->base,
+                                                     scatter->row0, scatter->Tblk, scatter->self, s))
+            return -1;
+        if (fold->sh_n > 0 &&
+            qe_launch_combine_sel(sc.ybuf + (size_t)sh0 * (k + 1) * H, sc.idx + (size_t)sh0 * k,
+                                  sc.score + (size_t)sh0 * k, fold->gate, 1, fold->sh_n, 0, k, c.hidden, 0, 1,
+                                  fold->sh_out, s))
+            return -1;
+        g_launches += (sh0 > 0) + (fold->sh_n > 0);
+        return 0;
     }
     if (scatter) {
         if (qe_launch_combine_sel_scatter(sc.ybuf, sc.idx, sc.score, n, k, c.hidden, scatter->base, scatter->row0,
@@ -1086,8 +1114,12 @@ int qe_moe_ep_combine_device(QeMoe *m, int T, const float *part, const int32_t *
 struct QeEpXchg {
     QeMoe *m;
     int G, self, Tmax, H, k;
-    char *mine;                      /* this rank's buffers: recv_x [G][Tmax][H], recv_meta [G][Tmax][2k], back [G][Tmax][H] */
-    size_t off_meta, off_back, bytes;
+    char *mine;                      /* this rank's buffers: recv_x [G+1][Tmax][H] (block G: its own rows, written by
+                                      * qe_moe_ep_route_p2p), recv_meta [G][Tmax][2k], back [G][Tmax][H],
+                                      * gate [Tmax] (own tokens' shared-expert gate logits), shared [Tmax][H] */
+    size_t off_meta, off_back, off_gate, off_shared, bytes;
+    int fold_T;                      /* T of a step routed by qe_moe_ep_route_p2p (shared expert in the expert
+                                      * stage), until its combine; else 0 */
     char *base[64];                  /* every rank's allocation as mapped here (own = mine)                      */
     bool opened[64];
     void **dptr;                     /* device arrays: recv_x[G], recv_meta[G], back[G]                          */
@@ -1125,9 +1157,11 @@ QeEpXchg *qe_ep_xchg_create(QeMoe *m, int T_max, void *handle) {
     x->H = m->cfg.hidden;
     x->k = m->cfg.top_k;
     const size_t rows = (size_t)x->G * T_max;
-    x->off_meta = align256(rows * x->H * 4);
+    x->off_meta = align256((rows + T_max) * x->H * 4);
     x->off_back = x->off_meta + align256(rows * 2 * x->k * 4);
-    x->bytes = x->off_back + align256(rows * x->H * 4);
+    x->off_gate = x->off_back + align256(rows * x->H * 4);
+    x->off_shared = x->off_gate + align256((size_t)T_max * 4);
+    x->bytes = x->off_shared + align256((size_t)T_max * x->H * 4);
     if (cudaMalloc((void **)&x->mine, x->bytes) != cudaSuccess ||
         cudaMalloc((void **)&x->dptr, sizeof(void *) * 3 * x->G) != cudaSuccess ||
         cudaIpcGetMemHandle((cudaIpcMemHandle_t *)handle, x->mine) != cudaSuccess) {
@@ -1206,26 +1240,61 @@ int qe_moe_ep_dispatch_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, const 
     return 0;
 }
 
+int qe_moe_ep_route_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, int32_t *meta, void *stream) {
+    if (!m || !xc || !x || !meta || T < 1 || T > xc->Tmax || T > m->cfg.max_tokens)
+        QE_FAIL("ep_route_p2p: bad arguments (T must be within the exchange's T_max and the handle's max_tokens)");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int k = m->cfg.top_k, G = m->cfg.ep_size, E = m->cfg.E;
+    const size_t H = m->cfg.hidden;
+    if (ensure_ws(d, scratch_layout(m->cfg, T, nullptr, nullptr))) return -1;
+    Scratch sc;
+    scratch_layout(m->cfg, T, (char *)d->ws, &sc);
+    if (run_route(m, x, T, sc, s)) return -1;
+    ep_meta_kernel<<<(T * k + 255) / 256, 256, 0, s>>>(sc.idx, sc.score, T, k, meta);
+    QE_CHECK(cudaGetLastError());
+    ep_gate_kernel<<<(T + 255) / 256, 256, 0, s>>>(sc.logits, T, E, (float *)(xc->mine + xc->off_gate));
+    QE_CHECK(cudaGetLastError());
+    QE_CHECK(cudaMemcpyAsync(xc->mine + (size_t)G * T * H * 4, x, sizeof(float) * (size_t)T * H,
+                             cudaMemcpyDeviceToDevice, s));
+    g_launches += 2;
+    xc->fold_T = T;
+    return 0;
+}
+
 int qe_moe_ep_experts_p2p(QeMoe *m, QeEpXchg *xc, int T, void *stream) {
     if (!m || !xc || T < 1 || T > xc->Tmax) QE_FAIL("ep_experts_p2p: bad arguments");
     DevCtx *d;
     if (dev_ctx(m->device, &d)) return -1;
     cudaStream_t s = (cudaStream_t)stream;
-    const int G = m->cfg.ep_size, n = G * T, P = std::min(n, m->cfg.max_tokens), k = m->cfg.top_k;
+    const bool fold = xc->fold_T == T;
+    const int G = m->cfg.ep_size, nr = G * T, n = nr + (fold ? T : 0), k = m->cfg.top_k;
+    const int P = std::min(n, m->cfg.max_tokens);
     const size_t H = m->cfg.hidden;
     if (ensure_ws(d, scratch_layout(m->cfg, P, nullptr, nullptr))) return -1;
     Scratch sc;
     scratch_layout(m->cfg, P, (char *)d->ws, &sc);
     const float *rx = (const float *)xc->mine;
     const int32_t *rm = (const int32_t *)(xc->mine + xc->off_meta);
+    const float *gate = (const float *)(xc->mine + xc->off_gate);
+    float *sh_out = (float *)(xc->mine + xc->off_shared);
     for (int r0 = 0; r0 < n; r0 += P) {
         const int cnt = std::min(P, n - r0);
-        ep_local_kernel<<<(cnt * k + 255) / 256, 256, 0, s>>>(rm + (size_t)r0 * 2 * k, cnt, k, m->e0, m->E_loc,
-                                                             sc.idx, sc.score);
-        QE_CHECK(cudaGetLastError());
+        const int cr = std::max(0, std::min(cnt, nr - r0));   /* received rows of this pass; the rest are own rows */
+        if (cr > 0) {
+            ep_local_kernel<<<(cr * k + 255) / 256, 256, 0, s>>>(rm + (size_t)r0 * 2 * k, cr, k, m->e0, m->E_loc,
+                                                                sc.idx, sc.score);
+            QE_CHECK(cudaGetLastError());
+            g_launches += 1;
+        }
+        if (cnt > cr) QE_CHECK(cudaMemsetAsync(sc.idx + (size_t)cr * k, 0xff, sizeof(int32_t) * (size_t)(cnt - cr) * k, s));
         const EpScatter sca = {(float *const *)(xc->dptr + 2 * G), r0, T, m->cfg.ep_rank};
-        if (run_experts(m, rx + (size_t)r0 * H, nullptr, cnt, sc, d->sms, true, false, s, &sca)) return -1;
-        g_launches += 1;
+        const int o0 = r0 + cr - nr;                          /* first own row of this pass */
+        const EpFold fo = {cr, cnt - cr, gate + std::max(0, o0), sh_out + (size_t)std::max(0, o0) * H};
+        if (run_experts(m, rx + (size_t)r0 * H, nullptr, cnt, sc, d->sms, true, false, s, &sca,
+                        fold ? &fo : nullptr))
+            return -1;
     }
     /* the partial rows written into the peers must be visible to them once this stream's work is done */
     return 0;
@@ -1234,6 +1303,13 @@ int qe_moe_ep_experts_p2p(QeMoe *m, QeEpXchg *xc, int T, void *stream) {
 int qe_moe_ep_combine_p2p(QeMoe *m, QeEpXchg *xc, int T, const int32_t *home, const float *shared, float *out,
                           void *stream) {
     if (!xc || T < 1 || T > xc->Tmax) QE_FAIL("ep_combine_p2p: bad arguments");
+    if (!shared) {
+        /* the step was routed by qe_moe_ep_route_p2p: the shared-expert term is in the exchange */
+        if (xc->fold_T != T) QE_FAIL("ep_combine_p2p: no shared term given and the step was not routed by "
+                                     "qe_moe_ep_route_p2p");
+        shared = (const float *)(xc->mine + xc->off_shared);
+    }
+    xc->fold_T = 0;
     return qe_moe_ep_combine_device(m, T, (const float *)(xc->mine + xc->off_back), home, shared, out, stream);
 }
 

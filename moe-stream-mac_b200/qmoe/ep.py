@@ -86,6 +86,10 @@ class DeviceEngine:
             lib().qe_ep_xchg_free(self.xchg)
             self.xchg = None
 
+    def route_p2p(self, x, meta):
+        if lib().qe_moe_ep_route_p2p(self.block.handle, self.xchg, x.shape[0], self._p(x), self._p(meta), self._s()):
+            raise EngineError("qe_moe_ep_route_p2p failed")
+
     def dispatch_p2p(self, x, meta, home, counts):
         if lib().qe_moe_ep_dispatch_p2p(self.block.handle, self.xchg, x.shape[0], self._p(x), self._p(meta),
                                         self._p(home), self._p(counts), self._s()):
@@ -141,18 +145,26 @@ class ExpertParallelMoe:
             dist.barrier(group=self.group)
             self.engine.xchg_free()
 
-    def forward(self, x: torch.Tensor, mode: str = "sharded", mark=None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, mode: str = "sharded", mark=None, fold: bool = True) -> torch.Tensor:
         """out[T][hidden] for this rank's x[T][hidden] (sharded), or for the tokens every rank holds
         (replicated). Every rank must call it with the same T and mode. mark(name), if given, is called
-        after each phase (route, pack, dispatch, experts, return, combine), e.g. to record CUDA events."""
+        after each phase (route, pack, dispatch, experts, return, combine), e.g. to record CUDA events.
+        p2p with fold (the default when (world + 1) * T fits the handle's max_tokens): the shared expert runs
+        on this rank's own rows inside the expert stage's launches (qe_moe_ep_route_p2p) instead of in a
+        separate pass during routing."""
         if mode not in ("sharded", "replicated", "p2p"):
             raise ValueError(f"mode {mode!r}")
         mark = mark or (lambda name: None)
         T, H, k, G = x.shape[0], self.hidden, self.top_k, self.world
         meta = self._empty(T, 2 * k, dtype=torch.int32)
-        shared = self._empty(T, H)
         out = self._empty(T, H)
-        self.engine.route(x, meta, shared)
+        fold = fold and mode == "p2p" and (G + 1) * T <= self.engine.block.cfg.max_tokens
+        if fold:
+            shared = None
+            self.engine.route_p2p(x, meta)
+        else:
+            shared = self._empty(T, H)
+            self.engine.route(x, meta, shared)
         mark("route")
         if mode == "replicated":
             partial = self._empty(T, H)

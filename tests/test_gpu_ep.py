@@ -57,8 +57,9 @@ def _emulated_sharded_step(blocks, xs):
     return outs, [m.cpu().numpy() for m in meta], [c.cpu().numpy() for c in counts]
 
 
-def _emulated_p2p_step(blocks, xs):
-    """The peer-memory step with G emulated ranks on one GPU (contexts connected with plain pointers)."""
+def _emulated_p2p_step(blocks, xs, fold=False):
+    """The peer-memory step with G emulated ranks on one GPU (contexts connected with plain pointers); fold:
+    routed by qe_moe_ep_route_p2p, the shared expert running in the expert stage's launches."""
     import ctypes as C
     from qmoe.ep import DeviceEngine
     from qmoe.lib import lib
@@ -75,14 +76,17 @@ def _emulated_p2p_step(blocks, xs):
     home = [torch.empty(G, T, dtype=torch.int32, device=dev) for _ in range(G)]
     counts = [torch.empty(G, dtype=torch.int32, device=dev) for _ in range(G)]
     for r in range(G):
-        eng[r].route(xs[r], meta[r], shared[r])
+        if fold:
+            eng[r].route_p2p(xs[r], meta[r])
+        else:
+            eng[r].route(xs[r], meta[r], shared[r])
         eng[r].dispatch_p2p(xs[r], meta[r], home[r], counts[r])
     for d in range(G):
         eng[d].experts_p2p(T)
     outs = []
     for r in range(G):
         out = torch.empty(T, H, device=dev)
-        eng[r].combine_p2p(T, home[r], shared[r], out)
+        eng[r].combine_p2p(T, home[r], None if fold else shared[r], out)
         outs.append(out)
     torch.cuda.synchronize()
     res = [o.cpu().numpy() for o in outs]
@@ -91,13 +95,17 @@ def _emulated_p2p_step(blocks, xs):
     return res
 
 
+@pytest.mark.parametrize("fold", [False, True])
 @pytest.mark.parametrize("G,T", [(1, 16), (2, 64), (4, 24), (8, 5)])
-def test_ep_p2p_emulated_equals_all_to_all(G, T):
+def test_ep_p2p_emulated_equals_all_to_all(G, T, fold):
+    """Bit-identical to the all_to_all step, also with the shared expert folded into the expert stage (the
+    same tcgen05 kernels and token tile width run it in both batches here, and every token is an independent
+    MMA column)."""
     blocks = _blocks(CFG, G)
     gen = torch.Generator().manual_seed(500 + G + T)
     xs = [torch.randn(T, CFG.hidden, generator=gen).cuda() for _ in range(G)]
     want, _, _ = _emulated_sharded_step(blocks, xs)
-    got = _emulated_p2p_step(blocks, xs)
+    got = _emulated_p2p_step(blocks, xs, fold)
     for r in range(G):
         assert np.array_equal(got[r].view(np.uint32), want[r].cpu().numpy().view(np.uint32)), f"rank {r}"
     for b in blocks:
@@ -176,13 +184,13 @@ def _nccl_worker(rank, world, port, mode, q):
     try:
         from qmoe.ep import ExpertParallelMoe
         ep = ExpertParallelMoe.on_gpu(CFG, rank, world, rank, seed=5)
-        if mode == "p2p":
+        if mode.startswith("p2p"):
             ep.enable_p2p(64)
         ref = qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, device=rank)
         T = 48
         gen = torch.Generator().manual_seed(1000 + (rank if mode != "replicated" else 0))
         x = torch.randn(T, CFG.hidden, generator=gen).cuda(rank)
-        out = ep.forward(x, mode=mode)
+        out = ep.forward(x, mode="p2p", fold=False) if mode == "p2p_unfolded" else ep.forward(x, mode=mode)
         want = torch.empty_like(x)
         ref.forward_device(T, x.data_ptr(), want.data_ptr(), torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
@@ -194,7 +202,7 @@ def _nccl_worker(rank, world, port, mode, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["sharded", "replicated", "p2p"])
+@pytest.mark.parametrize("mode", ["sharded", "replicated", "p2p", "p2p_unfolded"])
 def test_ep_nccl_two_gpus(mode):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")

@@ -7,7 +7,9 @@ One step = one forward of one MoE block over the configuration's token batch (co
 4-bit hidden-2048 block, the configuration the benchmark metric is quoted on). Four blocks with distinct
 weights (4 x 453 MB, far above the 126 MB L2) are used in rotation, so no step finds its weights in L2.
 `value` is device-timed (CUDA events on the launching stream, inputs resident in HBM); `e2e` is the same
-metric through the public host-buffer call qe_moe_forward (pinned host x in, host out back, every step).
+metric through the public host-buffer calls (pinned host x in, host out back, every step), with consecutive
+steps pipelined by qe_moe_forward_async (each step's copies under its neighbours' kernels); `e2e.sync_value`
+is the one-call-at-a-time figure of qe_moe_forward.
 Under torchrun (N > 1) the block is expert-parallel (qmoe.ep): rank r holds experts [r*E/N, (r+1)*E/N) of
 every block plus the replicated router and shared expert, routes its own 512 tokens, and exchanges rows and
 partial sums with all_to_all over NCCL (weak scaling: per-rank tokens fixed); value = tokens of all ranks /
@@ -414,18 +416,61 @@ def main():
             else:    # qe_moe_forward: host buffers in and out
                 blocks[bi].forward(xn, on)
 
-    for i in range(3):
-        e2e_step(i)
-    barrier()
-    t0 = time.perf_counter()
-    for i in range(ke):
-        e2e_step(i)
-    barrier()
-    e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
-    e2e_value = world * T * ke / float(te.item())
+    # pipelined: the same public calls with step i+1's input copy and step i-1's output copy running under step
+    # i's kernels (1 GPU: qe_moe_forward_async; N GPUs: copy streams around qmoe.ep.ExpertParallelMoe.forward)
+    copy_in, copy_out = torch.cuda.Stream(), torch.cuda.Stream()
+    xd2 = [torch.empty(T, cfg.hidden, device="cuda") for _ in range(2)]
+    ev_in, ev_comp = [torch.cuda.Event() for _ in range(2)], [torch.cuda.Event() for _ in range(2)]
+    n_async = [0]
+
+    def e2e_async_step(i):
+        sel = range(len(blocks)) if args.stack else [i % len(blocks)]
+        for bi in sel:
+            if ep:
+                j = n_async[0] & 1
+                cur = torch.cuda.current_stream()
+                if n_async[0] >= 2:
+                    copy_in.wait_event(ev_comp[j])     # slot j's input was read by its forward
+                with torch.cuda.stream(copy_in):
+                    xd2[j].copy_(xh, non_blocking=True)
+                    ev_in[j].record(copy_in)
+                cur.wait_event(ev_in[j])
+                o = models[bi].forward(xd2[j], mode=args.ep_mode)
+                ev_comp[j].record(cur)
+                copy_out.wait_event(ev_comp[j])
+                with torch.cuda.stream(copy_out):
+                    oh.copy_(o, non_blocking=True)
+                o.record_stream(copy_out)
+                n_async[0] += 1
+            else:
+                blocks[bi].forward_async(xn, on)
+
+    def e2e_async_wait():
+        if ep:
+            copy_out.synchronize()
+            torch.cuda.current_stream().synchronize()
+        else:
+            blocks[0].wait()
+
+    def timed_e2e(run, wait=None):
+        for i in range(3):
+            run(i)
+        if wait:
+            wait()
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(ke):
+            run(i)
+        if wait:
+            wait()
+        barrier()
+        te = torch.tensor([time.perf_counter() - t0], device="cuda")
+        if world > 1:
+            torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+        return world * T * ke / float(te.item())
+
+    e2e_sync_value = timed_e2e(e2e_step)
+    e2e_value = timed_e2e(e2e_async_step, e2e_async_wait)
 
     peak, peak_kind = hbm_peak()
     peak_source = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s")
@@ -468,7 +513,13 @@ def main():
                                            args.stack),
                            cuda_graph=use_graph),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * cfg.hidden,
-                    "d2h_bytes_per_step": 4 * T * cfg.hidden, "steps": ke, "timing": "host clock, max over ranks"},
+                    "d2h_bytes_per_step": 4 * T * cfg.hidden, "steps": ke,
+                    "timing": "host clock, max over ranks; consecutive steps pipelined: each step's pinned-host "
+                              "input copy and output copy run under its neighbours' kernels "
+                              + ("(copy streams around ExpertParallelMoe.forward)" if ep else "(qe_moe_forward_async)"),
+                    "sync_value": e2e_sync_value,
+                    "sync_timing": "one step at a time: copy in, forward, copy out, wait"
+                                   + (" (ExpertParallelMoe.forward)" if ep else " (qe_moe_forward)")},
             "roofline": roofline, "gpu_launches": launches, "clocks": clk}
     if args.stack:   # every token passes through all blocks of the stack: block-level throughput for reference
         line["block_tokens_per_s"] = value * args.blocks

@@ -90,6 +90,14 @@ void qe_moe_free(QeMoe *m);
  * Replaces T calls of moe_layer_step (engine/src/moe_layer.c:66-89). 0 ok, -1 error (out untouched).
  * A handle holding a subset of the experts (ep_size > 1) refuses it: use the qe_moe_ep_* calls. */
 int qe_moe_forward(QeMoe *m, int T, const float *x, float *out);
+/* Pipelined qe_moe_forward: enqueues the copy of x[T][hidden] to the device, the forward and the copy of
+ * out[T][hidden] back, and returns without waiting; qe_moe_forward_wait(m) waits for every such call on m's
+ * device. Consecutive calls overlap their copies with each other's kernels (two staging slots per device; x
+ * and out in pinned host memory for the copies to be asynchronous). x and out must stay valid and out unread
+ * until the wait. Same results as qe_moe_forward; T <= max_tokens; the routing trace and the read statistics
+ * are not updated. No reference counterpart (moe_layer_step returns with out written). 0 ok, -1 error. */
+int qe_moe_forward_async(QeMoe *m, int T, const float *x, float *out);
+int qe_moe_forward_wait(QeMoe *m);
 
 /* Same on device buffers of m's device, enqueued on `stream` (a cudaStream_t, NULL = legacy default),
  * no host synchronisation. */

@@ -43,6 +43,14 @@ struct DevCtx {
     void *ws = nullptr;       /* scratch workspace shared by all handles on this device */
     size_t ws_bytes = 0;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    /* pipelined host-buffer forwards (qe_moe_forward_async): copy-in and copy-out streams and two staging
+     * slots, each an x and an out buffer of stage_cap floats */
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    float *stage = nullptr;
+    size_t stage_cap = 0;
+    cudaEvent_t ev_h2d[2] = {}, ev_comp[2] = {}, ev_d2h[2] = {};
+    bool slot_used[2] = {false, false};
+    unsigned long long async_n = 0;
 };
 
 std::mutex g_mu;
@@ -964,6 +972,65 @@ void qe_moe_graph_free(QeMoeGraph *g) {
     cudaGraphDestroy(g->graph);
     cudaFree(g->ws);
     free(g);
+}
+
+/* Pipelined forward with host buffers. Call i uses staging slot i % 2: its x copy (copy-in stream) waits until
+ * the forward of call i - 2 has read the slot, its forward (the device stream) waits for the copy and for call
+ * i - 2's out copy, and its out copy (copy-out stream) waits for the forward. So the copies of neighbouring
+ * calls run under each other's kernels; every call computes what qe_moe_forward does. */
+int qe_moe_forward_async(QeMoe *m, int T, const float *x, float *out) {
+    if (!m || !x || !out || T < 1) QE_FAIL("forward_async: bad arguments");
+    if (m->cfg.ep_size > 1) QE_FAIL("forward_async: this handle holds experts [%d, %d) only: use the qe_moe_ep_* calls",
+                                    m->e0, m->e0 + m->E_loc);
+    if (T > m->cfg.max_tokens) QE_FAIL("forward_async: T=%d above the handle's max_tokens %d", T, m->cfg.max_tokens);
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    cudaStream_t s = d->stream;
+    if (ensure_ws(d, scratch_layout(m->cfg, T, nullptr, nullptr))) return -1;
+    if (!d->s_in) {
+        QE_CHECK(cudaStreamCreateWithFlags(&d->s_in, cudaStreamNonBlocking));
+        QE_CHECK(cudaStreamCreateWithFlags(&d->s_out, cudaStreamNonBlocking));
+        for (int j = 0; j < 2; j++) {
+            QE_CHECK(cudaEventCreateWithFlags(&d->ev_h2d[j], cudaEventDisableTiming));
+            QE_CHECK(cudaEventCreateWithFlags(&d->ev_comp[j], cudaEventDisableTiming));
+            QE_CHECK(cudaEventCreateWithFlags(&d->ev_d2h[j], cudaEventDisableTiming));
+        }
+    }
+    const size_t nf = (size_t)T * m->cfg.hidden;
+    if (d->stage_cap < nf) {
+        QE_CHECK(cudaDeviceSynchronize());   /* no call in flight uses the old staging memory */
+        if (d->stage) cudaFree(d->stage);
+        d->stage = nullptr;
+        d->stage_cap = 0;
+        QE_CHECK(cudaMalloc((void **)&d->stage, sizeof(float) * 4 * nf));
+        d->stage_cap = nf;
+        d->slot_used[0] = d->slot_used[1] = false;
+    }
+    Scratch sc;
+    scratch_layout(m->cfg, T, (char *)d->ws, &sc);
+    const int j = (int)(d->async_n++ & 1);
+    float *xd = d->stage + (size_t)(2 * j) * d->stage_cap, *od = xd + d->stage_cap;
+    if (d->slot_used[j]) QE_CHECK(cudaStreamWaitEvent(d->s_in, d->ev_comp[j], 0));
+    QE_CHECK(cudaMemcpyAsync(xd, x, sizeof(float) * nf, cudaMemcpyHostToDevice, d->s_in));
+    QE_CHECK(cudaEventRecord(d->ev_h2d[j], d->s_in));
+    QE_CHECK(cudaStreamWaitEvent(s, d->ev_h2d[j], 0));
+    if (d->slot_used[j]) QE_CHECK(cudaStreamWaitEvent(s, d->ev_d2h[j], 0));
+    if (run_pass(m, xd, od, T, sc, d->sms, s)) return -1;
+    QE_CHECK(cudaEventRecord(d->ev_comp[j], s));
+    QE_CHECK(cudaStreamWaitEvent(d->s_out, d->ev_comp[j], 0));
+    QE_CHECK(cudaMemcpyAsync(out, od, sizeof(float) * nf, cudaMemcpyDeviceToHost, d->s_out));
+    QE_CHECK(cudaEventRecord(d->ev_d2h[j], d->s_out));
+    d->slot_used[j] = true;
+    return 0;
+}
+
+int qe_moe_forward_wait(QeMoe *m) {
+    if (!m) QE_FAIL("forward_wait: bad arguments");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    if (d->s_out) QE_CHECK(cudaStreamSynchronize(d->s_out));
+    QE_CHECK(cudaStreamSynchronize(d->stream));
+    return 0;
 }
 
 int qe_moe_forward(QeMoe *m, int T, const float *x, float *out) {

@@ -103,6 +103,25 @@ class MoeBlock:
             raise EngineError("qe_moe_forward failed")
         return out
 
+    def forward_async(self, x: np.ndarray, out: np.ndarray) -> None:
+        """qe_moe_forward_async: enqueue the forward of host x[T][hidden] into host out (both C-contiguous
+        float32; pinned memory, e.g. torch's pin_memory().numpy(), for the copies to overlap the kernels).
+        out is written by the time wait() returns; both arrays are kept alive until then."""
+        if x.dtype != np.float32 or out.dtype != np.float32 or not x.flags.c_contiguous or not out.flags.c_contiguous \
+                or x.shape != out.shape or x.ndim != 2:
+            raise ValueError("x and out must be C-contiguous float32 [T][hidden] arrays of one shape")
+        self._inflight = getattr(self, "_inflight", [])
+        self._inflight.append((x, out))
+        if lib().qe_moe_forward_async(self.handle, x.shape[0], fptr(x), fptr(out)):
+            raise EngineError("qe_moe_forward_async failed")
+
+    def wait(self) -> None:
+        """qe_moe_forward_wait: every forward_async call on this block's device has written its out."""
+        rc = lib().qe_moe_forward_wait(self.handle)
+        self._inflight = []
+        if rc:
+            raise EngineError("qe_moe_forward_wait failed")
+
     def forward_device(self, T: int, x_ptr: int, out_ptr: int, stream: int = 0) -> None:
         if lib().qe_moe_forward_device(self.handle, T, C.c_void_p(x_ptr), C.c_void_p(out_ptr), C.c_void_p(stream)):
             raise EngineError("qe_moe_forward_device failed")

@@ -72,6 +72,8 @@ def lib() -> C.CDLL:
         L.qe_device_error.restype = C.c_int
         L.qe_route_f32_noalloc.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp]
         L.qe_moe_ep_route_device.argtypes = [vp, C.c_int, vp, vp, vp, vp]
+        L.qe_moe_forward_async.argtypes = [vp, C.c_int, vp, vp]
+        L.qe_moe_forward_wait.argtypes = [vp]
         L.qe_moe_ep_pack_device.argtypes = [vp, C.c_int, vp, vp, vp, vp, vp, vp, vp]
         L.qe_moe_ep_experts_device.argtypes = [vp, C.c_int, vp, vp, vp, vp]
         L.qe_moe_ep_combine_device.argtypes = [vp, C.c_int, vp, vp, vp, vp, vp]

@@ -296,7 +296,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
-                    help="1 GPU: replay each block's forward as a captured CUDA graph (auto: decode batches, T <= 4)")
+                    help="1 GPU: replay each block's forward as a captured CUDA graph (qe_moe_graph_create; auto: "
+                         "on) or launch its kernels one by one (off)")
     ap.add_argument("--ep-mode", default="p2p", choices=["p2p", "sharded"],
                     help="N > 1: exchange through peer memory (p2p) or NCCL all_to_all (sharded)")
     args = ap.parse_args()
@@ -351,7 +352,7 @@ def main():
             else:
                 blocks[i % len(blocks)].forward_device(T, x.data_ptr(), out.data_ptr(), sptr)
 
-        use_graph = args.graph == "on" or (args.graph == "auto" and T <= 4)
+        use_graph = args.graph in ("on", "auto")
         if use_graph:   # one captured forward per block, replayed (no per-kernel host launch cost)
             graphs = [b.graph(T, x.data_ptr(), out.data_ptr()) for b in blocks]
             eager_step = step
@@ -453,7 +454,8 @@ def main():
             blocks[0].wait()
 
     def timed_e2e(run, wait=None):
-        for i in range(3):
+        # warm-up: every block at least twice (each block's first pipelined call captures its CUDA graph)
+        for i in range(max(3, 2 * len(blocks) + 1)):
             run(i)
         if wait:
             wait()

@@ -509,16 +509,29 @@ __global__ void combine4_kernel(const float *__restrict__ ybuf, const float *__r
     const int t = (int)(i / H4), j4 = (int)(i % H4);
     const float4 *y = reinterpret_cast<const float4 *>(ybuf + (size_t)t * (k + 1) * H) + j4;
     float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int s = 0; s < k; s++) {
-        const float sc = score[(size_t)t * k + s];
-        const float4 v = y[(size_t)s * H4];
-        o.x = __fadd_rn(o.x, __fmul_rn(sc, v.x));
-        o.y = __fadd_rn(o.y, __fmul_rn(sc, v.y));
-        o.z = __fadd_rn(o.z, __fmul_rn(sc, v.z));
-        o.w = __fadd_rn(o.w, __fmul_rn(sc, v.w));
+    /* the slots' rows in batches of 8 independent loads (the shared expert's row with the last batch), then
+     * added in slot order */
+    const float4 vsh = y[(size_t)k * H4];
+    for (int s0 = 0; s0 < k; s0 += 8) {
+        float4 v[8];
+        float sc[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+            if (s0 + u < k) {
+                v[u] = y[(size_t)(s0 + u) * H4];
+                sc[u] = score[(size_t)t * k + s0 + u];
+            }
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+            if (s0 + u < k) {
+                o.x = __fadd_rn(o.x, __fmul_rn(sc[u], v[u].x));
+                o.y = __fadd_rn(o.y, __fmul_rn(sc[u], v[u].y));
+                o.z = __fadd_rn(o.z, __fmul_rn(sc[u], v[u].z));
+                o.w = __fadd_rn(o.w, __fmul_rn(sc[u], v[u].w));
+            }
     }
     const float sg = qe_sigmoid(logits[(size_t)t * ld_logits + E]);
-    const float4 v = y[(size_t)k * H4];
+    const float4 v = vsh;
     o.x = __fadd_rn(o.x, __fmul_rn(sg, v.x));
     o.y = __fadd_rn(o.y, __fmul_rn(sg, v.y));
     o.z = __fadd_rn(o.z, __fmul_rn(sg, v.z));

@@ -191,6 +191,9 @@ struct QeMoe {
     bool decode;            /* decode GEMVs available for this shape */
     bool group;             /* grouped GEMVs available for this shape */
     int tile;               /* tensor-core token tile: 0 = by load, else 32 or 64 (QE_TC_TILE) */
+    QeMoeGraph *agraph[2];  /* qe_moe_forward_async: the forward captured per staging slot, for a_T, a_x, a_o */
+    int a_T[2];
+    const float *a_x[2], *a_o[2];
     bool fused;             /* decode steps as one cooperative launch (QE_DECODE_FUSED=1; measured slower than
                              * the four launches replayed from a CUDA graph, so off by default) */
     alignas(64) unsigned char maps_gu[2 * 2 * 3 * 128];  /* [routed/shared][gate/up][codes, scales, biases] */
@@ -498,6 +501,8 @@ void qe_moe_free(QeMoe *m) {
     std::lock_guard<std::mutex> lock(g_mu);
     cudaSetDevice(m->device);
     cudaStreamSynchronize(g_dev[m->device].stream);
+    if (g_dev[m->device].s_out) cudaStreamSynchronize(g_dev[m->device].s_out);
+    for (int j = 0; j < 2; j++) qe_moe_graph_free(m->agraph[j]);
     cudaFree(m->weights);
     free(m);
 }
@@ -1010,12 +1015,28 @@ int qe_moe_forward_async(QeMoe *m, int T, const float *x, float *out) {
     scratch_layout(m->cfg, T, (char *)d->ws, &sc);
     const int j = (int)(d->async_n++ & 1);
     float *xd = d->stage + (size_t)(2 * j) * d->stage_cap, *od = xd + d->stage_cap;
+    /* the forward replayed from a CUDA graph captured for this slot and T (no per-kernel launch gaps): captured
+     * on first use, with the device idle, since the capture runs an eager forward on the slot's buffers */
+    static const bool use_graph = !getenv("QE_ASYNC_GRAPH") || strcmp(getenv("QE_ASYNC_GRAPH"), "0") != 0;
+    if (use_graph && !(m->agraph[j] && m->a_T[j] == T && m->a_x[j] == xd && m->a_o[j] == od)) {
+        QE_CHECK(cudaDeviceSynchronize());
+        qe_moe_graph_free(m->agraph[j]);
+        m->agraph[j] = qe_moe_graph_create(m, T, xd, od);
+        if (!m->agraph[j]) QE_FAIL("forward_async: graph capture failed");
+        m->a_T[j] = T;
+        m->a_x[j] = xd;
+        m->a_o[j] = od;
+    }
     if (d->slot_used[j]) QE_CHECK(cudaStreamWaitEvent(d->s_in, d->ev_comp[j], 0));
     QE_CHECK(cudaMemcpyAsync(xd, x, sizeof(float) * nf, cudaMemcpyHostToDevice, d->s_in));
     QE_CHECK(cudaEventRecord(d->ev_h2d[j], d->s_in));
     QE_CHECK(cudaStreamWaitEvent(s, d->ev_h2d[j], 0));
     if (d->slot_used[j]) QE_CHECK(cudaStreamWaitEvent(s, d->ev_d2h[j], 0));
-    if (run_pass(m, xd, od, T, sc, d->sms, s)) return -1;
+    if (use_graph) {
+        if (qe_moe_graph_launch(m->agraph[j], s)) return -1;
+    } else if (run_pass(m, xd, od, T, sc, d->sms, s)) {
+        return -1;
+    }
     QE_CHECK(cudaEventRecord(d->ev_comp[j], s));
     QE_CHECK(cudaStreamWaitEvent(d->s_out, d->ev_comp[j], 0));
     QE_CHECK(cudaMemcpyAsync(out, od, sizeof(float) * nf, cudaMemcpyDeviceToHost, d->s_out));

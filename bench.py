@@ -454,8 +454,9 @@ def main():
             blocks[0].wait()
 
     def timed_e2e(run, wait=None):
-        # warm-up: every block at least twice (each block's first pipelined call captures its CUDA graph)
-        for i in range(max(3, 2 * len(blocks) + 1)):
+        # warm-up: every block at least twice (each block's first pipelined call captures its CUDA graph); a
+        # --stack step already runs every block
+        for i in range(3 if args.stack else max(3, 2 * len(blocks) + 1)):
             run(i)
         if wait:
             wait()

@@ -326,6 +326,7 @@ def main():
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
     use_graph = False
+    graph_launches = [0]   # kernels launched by replays of torch-captured graphs (not seen by the library)
     if ep:
         from qmoe.ep import ExpertParallelMoe
         models = [ExpertParallelMoe.on_gpu(cfg, rank, world, local, seed=b + 1, block=b, max_tokens=(world + 1) * T)
@@ -341,6 +342,31 @@ def main():
                     mdl.forward(x, mode=args.ep_mode)
             else:
                 models[i % len(models)].forward(x, mode=args.ep_mode)
+
+        if args.ep_mode == "p2p" and args.graph in ("on", "auto"):
+            # the peer-memory step holds only this library's kernels (the barriers are qe_ep_xchg_barrier): after
+            # two eager passes (buffers and kernel attributes in place), each block's step is captured once and
+            # replayed; the kernels a replay launches are counted from the capture
+            for _ in range(2):
+                for mdl in models:
+                    mdl.forward(x, mode="p2p")
+            torch.cuda.synchronize()
+            torch.distributed.barrier()
+            ep_graphs = []
+            for mdl in models:
+                l0 = qmoe.kernel_launches()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                    g_out = mdl.forward(x, mode="p2p")
+                ep_graphs.append((g, g_out, qmoe.kernel_launches() - l0))
+            torch.cuda.synchronize()
+            use_graph = True
+            eager_step = step
+
+            def step(i):
+                for g, _, n in (ep_graphs if args.stack else [ep_graphs[i % len(ep_graphs)]]):
+                    g.replay()
+                    graph_launches[0] += n
     else:
         blocks = [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size,
                                 max_tokens=T, device=local, seed=b + 1, block=b) for b in range(args.blocks)]
@@ -375,7 +401,7 @@ def main():
     for i in range(max(args.warmup, 3)):
         step(i)
     barrier()
-    launches0 = qmoe.kernel_launches()
+    launches0 = qmoe.kernel_launches() + graph_launches[0]
     qmoe.profile_begin(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks.mark(True)
@@ -385,7 +411,7 @@ def main():
     e1.record(stream)
     barrier()
     clocks.mark(False)
-    launches = qmoe.kernel_launches() - launches0
+    launches = qmoe.kernel_launches() + graph_launches[0] - launches0
     stage_ms, passes = qmoe.profile_end(local)
     clk = clocks.stop()
     if not ep and use_graph:   # graphs carry no stage events: profile the same forwards eagerly, untimed
@@ -533,9 +559,12 @@ def main():
             cb["sample"] += f"; one block timed, value divided by the stack's {args.blocks} blocks"
         line["cpu_baseline"] = cb if cb else {"value": None, "unavailable": "oracle/_ref missing"}
     if ep:
+        if use_graph:   # the captured steps reference the exchange buffers: drop them before those are freed
+            torch.cuda.synchronize()
+            ep_graphs.clear()
         for mdl in models:
             mdl.close()
-    if use_graph:
+    elif use_graph:
         for g in graphs:
             g.close()
     for b in blocks:

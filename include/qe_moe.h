@@ -174,6 +174,13 @@ int qe_ep_xchg_connect_local(QeEpXchg *const *all, int n);
 void qe_ep_xchg_free(QeEpXchg *x);
 int qe_moe_ep_dispatch_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, const int32_t *meta, int32_t *home,
                            int32_t *counts, void *stream);
+/* A barrier across the ranks on the stream, in place of the caller's collective: every rank's work before it
+ * on its stream (its stores into the peers' buffers included) is complete and visible before any rank's work
+ * after it. One warp per rank publishes an epoch into each peer's flag slot and waits for every peer's, at
+ * most 2 s; the epoch is a device counter, so the call can be captured in a CUDA graph and replayed. Every
+ * rank must make the same sequence of calls, each on its own GPU (ranks emulated on one GPU must not use it:
+ * a wait on a kernel of the same GPU may never end). A timeout is reported by qe_device_error() (200 + 1). */
+int qe_ep_xchg_barrier(QeEpXchg *x, void *stream);
 int qe_moe_ep_route_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, int32_t *meta, void *stream);
 int qe_moe_ep_experts_p2p(QeMoe *m, QeEpXchg *xc, int T, void *stream);
 int qe_moe_ep_combine_p2p(QeMoe *m, QeEpXchg *xc, int T, const int32_t *home, const float *shared, float *out,
@@ -230,7 +237,9 @@ int qe_profile_begin(int device);
 int qe_profile_end(int device, double *stage_ms, int *passes);
 /* Kernels launched by this library since process start. */
 unsigned long long qe_kernel_launches(void);
-/* Nonzero if a tensor-core kernel's pipeline wait timed out (it then returned early; outputs invalid). */
+/* Nonzero if a bounded wait on the device timed out (the kernel then returned early; outputs invalid): a
+ * tensor-core kernel's pipeline wait (its code), the fused decode step's grid barrier (100 + code), or the
+ * exchange barrier of qe_ep_xchg_barrier (201). */
 int qe_device_error(void);
 
 #ifdef __cplusplus

@@ -1204,8 +1204,10 @@ struct QeEpXchg {
     int G, self, Tmax, H, k;
     char *mine;                      /* this rank's buffers: recv_x [G+1][Tmax][H] (block G: its own rows, written by
                                       * qe_moe_ep_route_p2p), recv_meta [G][Tmax][2k], back [G][Tmax][H],
-                                      * gate [Tmax] (own tokens' shared-expert gate logits), shared [Tmax][H] */
-    size_t off_meta, off_back, off_gate, off_shared, bytes;
+                                      * gate [Tmax] (own tokens' shared-expert gate logits), shared [Tmax][H],
+                                      * flags [1 + G] u32 (qe_ep_xchg_barrier: epoch counter, then one slot per
+                                      * rank written by that rank) */
+    size_t off_meta, off_back, off_gate, off_shared, off_flags, bytes;
     int fold_T;                      /* T of a step routed by qe_moe_ep_route_p2p (shared expert in the expert
                                       * stage), until its combine; else 0 */
     char *base[64];                  /* every rank's allocation as mapped here (own = mine)                      */
@@ -1215,6 +1217,44 @@ struct QeEpXchg {
 };
 
 namespace {
+__device__ int g_ep_error;   /* first exchange-barrier timeout, read by qe_device_error() */
+
+__device__ __forceinline__ uint64_t ep_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+/* Barrier across the ranks of the peer-memory exchange, one warp. The epoch is this rank's counter flags[self][0]
+ * plus one (every rank calls the barrier the same number of times, so the counters agree, also when the call
+ * is replayed from a CUDA graph). Lane r publishes the epoch into rank r's slot for this rank, after a system
+ * fence that orders this stream's earlier stores into the peers' buffers; then lane r waits, for at most
+ * wait_ns, until rank r's slot in this rank's flags reaches the epoch (a slot only grows). On timeout it
+ * records g_ep_error and returns. */
+__global__ void ep_barrier_kernel(unsigned *const *__restrict__ flags, int self, int G, unsigned long long wait_ns) {
+    const int lane = threadIdx.x;
+    unsigned *mine = flags[self];
+    const unsigned epoch = *(volatile unsigned *)mine + 1u;
+    __syncwarp();
+    __threadfence_system();
+    if (lane < G) asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flags[lane] + 1 + self), "r"(epoch) : "memory");
+    if (lane < G) {
+        const uint64_t t0 = ep_timer_ns();
+        for (;;) {
+            unsigned v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + 1 + lane) : "memory");
+            if ((int)(v - epoch) >= 0) break;
+            if (ep_timer_ns() - t0 > wait_ns) {
+                atomicCAS(&g_ep_error, 0, 1);
+                break;
+            }
+        }
+    }
+    __syncwarp();
+    if (lane == 0) *(volatile unsigned *)mine = epoch;
+    __threadfence_system();
+}
+
 /* The three buffers are laid out for the step's T (blocks of T rows), within the Tmax capacity. */
 void xchg_tables(QeEpXchg *x, int T, void **host) {
     for (int r = 0; r < x->G; r++) {
@@ -1222,6 +1262,7 @@ void xchg_tables(QeEpXchg *x, int T, void **host) {
         host[r] = b;
         host[x->G + r] = b + x->off_meta;
         host[2 * x->G + r] = b + x->off_back;
+        host[3 * x->G + r] = b + x->off_flags;
     }
     (void)T;
 }
@@ -1249,9 +1290,11 @@ QeEpXchg *qe_ep_xchg_create(QeMoe *m, int T_max, void *handle) {
     x->off_back = x->off_meta + align256(rows * 2 * x->k * 4);
     x->off_gate = x->off_back + align256(rows * x->H * 4);
     x->off_shared = x->off_gate + align256((size_t)T_max * 4);
-    x->bytes = x->off_shared + align256((size_t)T_max * x->H * 4);
+    x->off_flags = x->off_shared + align256((size_t)T_max * x->H * 4);
+    x->bytes = x->off_flags + align256(sizeof(unsigned) * (1 + (size_t)x->G));
     if (cudaMalloc((void **)&x->mine, x->bytes) != cudaSuccess ||
-        cudaMalloc((void **)&x->dptr, sizeof(void *) * 3 * x->G) != cudaSuccess ||
+        cudaMalloc((void **)&x->dptr, sizeof(void *) * 4 * x->G) != cudaSuccess ||
+        cudaMemset(x->mine + x->off_flags, 0, sizeof(unsigned) * (1 + (size_t)x->G)) != cudaSuccess ||
         cudaIpcGetMemHandle((cudaIpcMemHandle_t *)handle, x->mine) != cudaSuccess) {
         fprintf(stderr, "qengine_b200: ep_xchg_create: cannot allocate or export %zu bytes\n", x->bytes);
         if (x->mine) cudaFree(x->mine);
@@ -1277,9 +1320,9 @@ int qe_ep_xchg_connect(QeEpXchg *x, const void *handles) {
         x->base[r] = (char *)p;
         x->opened[r] = true;
     }
-    void *host[3 * 64];
+    void *host[4 * 64];
     xchg_tables(x, 0, host);
-    QE_CHECK(cudaMemcpy(x->dptr, host, sizeof(void *) * 3 * x->G, cudaMemcpyHostToDevice));
+    QE_CHECK(cudaMemcpy(x->dptr, host, sizeof(void *) * 4 * x->G, cudaMemcpyHostToDevice));
     return 0;
 }
 
@@ -1290,10 +1333,10 @@ int qe_ep_xchg_connect_local(QeEpXchg *const *all, int n) {
         QeEpXchg *x = all[i];
         if (!x || x->G != n) QE_FAIL("ep_xchg_connect_local: %d contexts for ep_size %d", n, x ? x->G : -1);
         for (int r = 0; r < n; r++) x->base[r] = all[r]->mine;
-        void *host[3 * 64];
+        void *host[4 * 64];
         xchg_tables(x, 0, host);
         QE_CHECK(cudaSetDevice(x->m->device));
-        QE_CHECK(cudaMemcpy(x->dptr, host, sizeof(void *) * 3 * x->G, cudaMemcpyHostToDevice));
+        QE_CHECK(cudaMemcpy(x->dptr, host, sizeof(void *) * 4 * x->G, cudaMemcpyHostToDevice));
     }
     return 0;
 }
@@ -1307,6 +1350,17 @@ void qe_ep_xchg_free(QeEpXchg *x) {
     cudaFree(x->dptr);
     cudaFree(x->mine);
     free(x);
+}
+
+int qe_ep_xchg_barrier(QeEpXchg *x, void *stream) {
+    if (!x) QE_FAIL("ep_xchg_barrier: bad arguments");
+    if (x->G > 32) QE_FAIL("ep_xchg_barrier: %d ranks (one warp serves at most 32)", x->G);
+    QE_CHECK(cudaSetDevice(x->m->device));
+    ep_barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((unsigned *const *)(x->dptr + 3 * x->G), x->self, x->G,
+                                                         2000000000ull);
+    QE_CHECK(cudaGetLastError());
+    g_launches += 1;
+    return 0;
 }
 
 int qe_moe_ep_dispatch_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, const int32_t *meta, int32_t *home,
@@ -1519,7 +1573,9 @@ unsigned long long qe_kernel_launches(void) { return g_launches.load(); }
 
 int qe_device_error(void) {
     const int t = qe_tc_error(), d = qe_decode_error();
-    return t ? t : d ? 100 + d : 0;
+    int e = 0;
+    if (cudaMemcpyFromSymbol(&e, g_ep_error, sizeof(int)) != cudaSuccess) return -1;
+    return t ? t : d ? 100 + d : e ? 200 + e : 0;
 }
 
 double qe_expert_gb_read(void) { return (double)g_bytes_read.load() / 1e9; }

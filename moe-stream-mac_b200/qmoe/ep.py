@@ -86,6 +86,10 @@ class DeviceEngine:
             lib().qe_ep_xchg_free(self.xchg)
             self.xchg = None
 
+    def xchg_barrier(self):
+        if lib().qe_ep_xchg_barrier(self.xchg, self._s()):
+            raise EngineError("qe_ep_xchg_barrier failed")
+
     def route_p2p(self, x, meta):
         if lib().qe_moe_ep_route_p2p(self.block.handle, self.xchg, x.shape[0], self._p(x), self._p(meta), self._s()):
             raise EngineError("qe_moe_ep_route_p2p failed")
@@ -125,8 +129,13 @@ class ExpertParallelMoe:
     def _empty(self, *shape, dtype=torch.float32):
         return torch.empty(*shape, dtype=dtype, device=self.device)
 
-    def enable_p2p(self, t_max: int) -> None:
-        """Create this rank's exchange buffers and map every other rank's (collective: all ranks call it)."""
+    def enable_p2p(self, t_max: int, barrier: str = "device") -> None:
+        """Create this rank's exchange buffers and map every other rank's (collective: all ranks call it).
+        barrier: "device" (qe_ep_xchg_barrier through the exchange's flags; the step then holds no NCCL call and
+        can be captured in a CUDA graph) or "nccl" (a one-element all_reduce)."""
+        if barrier not in ("device", "nccl"):
+            raise ValueError(f"barrier {barrier!r}")
+        self.barrier_kind = barrier
         h = self.engine.xchg_create(t_max)
         mine = torch.tensor(list(h), dtype=torch.uint8, device=self.device)
         allh = torch.empty(self.world * len(h), dtype=torch.uint8, device=self.device)
@@ -137,7 +146,11 @@ class ExpertParallelMoe:
         dist.barrier(group=self.group)
 
     def _barrier(self) -> None:
-        dist.all_reduce(self._flag, group=self.group)   # stream-ordered: every rank's preceding kernels are done
+        """Stream-ordered: every rank's preceding kernels are done (and their peer stores visible)."""
+        if getattr(self, "barrier_kind", "nccl") == "device":
+            self.engine.xchg_barrier()
+        else:
+            dist.all_reduce(self._flag, group=self.group)
 
     def close(self) -> None:
         if getattr(self.engine, "xchg", None):

@@ -86,6 +86,7 @@ def lib() -> C.CDLL:
         L.qe_ep_xchg_free.argtypes = [vp]
         L.qe_moe_ep_dispatch_p2p.argtypes = [vp, vp, C.c_int, vp, vp, vp, vp, vp]
         L.qe_moe_ep_route_p2p.argtypes = [vp, vp, C.c_int, vp, vp, vp]
+        L.qe_ep_xchg_barrier.argtypes = [vp, vp]
         L.qe_moe_ep_experts_p2p.argtypes = [vp, vp, C.c_int, vp]
         L.qe_moe_ep_combine_p2p.argtypes = [vp, vp, C.c_int, vp, vp, vp, vp]
         L.qe_moe_graph_create.restype = vp

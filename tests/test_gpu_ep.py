@@ -185,16 +185,40 @@ def _nccl_worker(rank, world, port, mode, q):
         from qmoe.ep import ExpertParallelMoe
         ep = ExpertParallelMoe.on_gpu(CFG, rank, world, rank, seed=5)
         if mode.startswith("p2p"):
-            ep.enable_p2p(64)
+            ep.enable_p2p(64, barrier="nccl" if mode == "p2p_unfolded" else "device")
         ref = qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, device=rank)
         T = 48
         gen = torch.Generator().manual_seed(1000 + (rank if mode != "replicated" else 0))
         x = torch.randn(T, CFG.hidden, generator=gen).cuda(rank)
-        out = ep.forward(x, mode="p2p", fold=False) if mode == "p2p_unfolded" else ep.forward(x, mode=mode)
-        want = torch.empty_like(x)
-        ref.forward_device(T, x.data_ptr(), want.data_ptr(), torch.cuda.current_stream().cuda_stream)
-        torch.cuda.synchronize()
-        q.put((rank, float(_rel(out.cpu().numpy(), want.cpu().numpy()).max())))
+
+        def reference(xv):
+            want = torch.empty_like(xv)
+            ref.forward_device(T, xv.data_ptr(), want.data_ptr(), torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            return want.cpu().numpy()
+
+        if mode == "p2p_graph":
+            # the peer-memory step with device barriers, captured once and replayed on new inputs
+            for _ in range(2):
+                ep.forward(x, mode="p2p")
+            torch.cuda.synchronize()
+            dist.barrier()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                g_out = ep.forward(x, mode="p2p")
+            worst = 0.0
+            for _ in range(3):
+                x.copy_(torch.randn(T, CFG.hidden, generator=gen).cuda(rank))
+                g.replay()
+                torch.cuda.synchronize()
+                worst = max(worst, float(_rel(g_out.cpu().numpy(), reference(x)).max()))
+            del g, g_out
+            torch.cuda.synchronize()
+            q.put((rank, worst, qmoe.lib().qe_device_error()))
+        else:
+            out = ep.forward(x, mode="p2p", fold=False) if mode == "p2p_unfolded" else ep.forward(x, mode=mode)
+            torch.cuda.synchronize()
+            q.put((rank, float(_rel(out.cpu().numpy(), reference(x)).max()), qmoe.lib().qe_device_error()))
         ep.close()
         dist.barrier()
     finally:
@@ -202,8 +226,11 @@ def _nccl_worker(rank, world, port, mode, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["sharded", "replicated", "p2p", "p2p_unfolded"])
+@pytest.mark.parametrize("mode", ["sharded", "replicated", "p2p", "p2p_unfolded", "p2p_graph"])
 def test_ep_nccl_two_gpus(mode):
+    """One process per GPU over NCCL against the single-handle forward. p2p: peer-memory exchange with the
+    library's device barriers; p2p_unfolded: the separate shared-expert pass and NCCL barriers; p2p_graph: the
+    device-barrier step captured in a CUDA graph and replayed on new inputs."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -221,5 +248,6 @@ def test_ep_nccl_two_gpus(mode):
             p.kill()
     assert codes == [0, 0], codes
     for _ in procs:
-        rank, rel = q.get(timeout=10)
+        rank, rel, err = q.get(timeout=10)
+        assert err == 0, (rank, err)
         assert rel <= 5e-6, (rank, rel)

@@ -12,8 +12,9 @@ steps pipelined by qe_moe_forward_async (each step's copies under its neighbours
 is the one-call-at-a-time figure of qe_moe_forward.
 Under torchrun (N > 1) the block is expert-parallel (qmoe.ep): rank r holds experts [r*E/N, (r+1)*E/N) of
 every block plus the replicated router and shared expert, routes its own 512 tokens, and exchanges rows and
-partial sums with all_to_all over NCCL (weak scaling: per-rank tokens fixed); value = tokens of all ranks /
-max rank time.
+partial sums through peer memory (the kernels store into the other GPUs' buffers; --ep-mode sharded: all_to_all
+over NCCL), weak scaling (per-rank tokens fixed); value = tokens of all ranks / max rank time. With the
+peer-memory exchange each block's step is replayed from a CUDA graph, as on one GPU.
 --impl reference times the reference's own C engine (oracle/_ref, built from its sources) on the host.
 """
 from __future__ import annotations
@@ -449,6 +450,16 @@ def main():
     xd2 = [torch.empty(T, cfg.hidden, device="cuda") for _ in range(2)]
     ev_in, ev_comp = [torch.cuda.Event() for _ in range(2)], [torch.cuda.Event() for _ in range(2)]
     n_async = [0]
+    e2e_graphs, ev_out, out_used = {}, {}, set()
+    if ep and use_graph:   # the captured step per block and input slot (as the timed steps replay theirs)
+        for bi, mdl in enumerate(models):
+            for j in range(2):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                    g_out = mdl.forward(xd2[j], mode="p2p")
+                e2e_graphs[(bi, j)] = (g, g_out)
+                ev_out[(bi, j)] = torch.cuda.Event()
+        torch.cuda.synchronize()
 
     def e2e_async_step(i):
         sel = range(len(blocks)) if args.stack else [i % len(blocks)]
@@ -462,12 +473,22 @@ def main():
                     xd2[j].copy_(xh, non_blocking=True)
                     ev_in[j].record(copy_in)
                 cur.wait_event(ev_in[j])
-                o = models[bi].forward(xd2[j], mode=args.ep_mode)
+                if e2e_graphs:
+                    g, o = e2e_graphs[(bi, j)]
+                    if (bi, j) in out_used:
+                        cur.wait_event(ev_out[(bi, j)])   # the last copy of this graph's output has finished
+                    g.replay()
+                else:
+                    o = models[bi].forward(xd2[j], mode=args.ep_mode)
                 ev_comp[j].record(cur)
                 copy_out.wait_event(ev_comp[j])
                 with torch.cuda.stream(copy_out):
                     oh.copy_(o, non_blocking=True)
-                o.record_stream(copy_out)
+                    if e2e_graphs:
+                        ev_out[(bi, j)].record(copy_out)
+                        out_used.add((bi, j))
+                if not e2e_graphs:
+                    o.record_stream(copy_out)
                 n_async[0] += 1
             else:
                 blocks[bi].forward_async(xn, on)
@@ -545,7 +566,8 @@ def main():
                     "d2h_bytes_per_step": 4 * T * cfg.hidden, "steps": ke,
                     "timing": "host clock, max over ranks; consecutive steps pipelined: each step's pinned-host "
                               "input copy and output copy run under its neighbours' kernels "
-                              + ("(copy streams around ExpertParallelMoe.forward)" if ep else "(qe_moe_forward_async)"),
+                              + ("(copy streams around ExpertParallelMoe.forward, replayed from CUDA graphs when the "
+                                 "timed steps are)" if ep else "(qe_moe_forward_async)"),
                     "sync_value": e2e_sync_value,
                     "sync_timing": "one step at a time: copy in, forward, copy out, wait"
                                    + (" (ExpertParallelMoe.forward)" if ep else " (qe_moe_forward)")},
@@ -562,6 +584,7 @@ def main():
         if use_graph:   # the captured steps reference the exchange buffers: drop them before those are freed
             torch.cuda.synchronize()
             ep_graphs.clear()
+            e2e_graphs.clear()
         for mdl in models:
             mdl.close()
     elif use_graph:

@@ -34,6 +34,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "moe-stream-mac_b200"))
 
 import numpy as np  # noqa: E402
+from qmoe.synth import CONFIGS  # noqa: E402
 
 METRIC = "MoE-layer tokens/s"
 PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
@@ -53,10 +54,13 @@ def hbm_peak():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 50 ms while the timed region runs."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms from start to stop (warm-up, timed steps, e2e
+    passes and sub-records alike); mark(name, start) brackets named phases, and stop() reports the samples inside
+    any phase (median SM clock, reasons) plus a per-phase breakdown."""
     Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, gpu: int):
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
@@ -65,13 +69,26 @@ class ClockSampler:
                                        "-lms", "50", "-i", str(gpu)], stdout=self.f, stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.p = None
-        self.t0 = self.t1 = None
+        self.phases = []   # [name, t0, t1]
 
-    def mark(self, start: bool):
+    def mark(self, name: str, start: bool):
         if start:
-            self.t0 = time.time()
+            self.phases.append([name, time.time(), None])
         else:
-            self.t1 = time.time()
+            for ph in reversed(self.phases):
+                if ph[0] == name and ph[2] is None:
+                    ph[2] = time.time()
+                    break
+
+    def _summary(self, rows):
+        sm = [float(r[2]) for r in rows]
+        reasons = set()
+        for r in rows:
+            for n, v in zip(self.NAMES, r[6:10]):
+                if v.strip() == "Active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][3]), "reasons": sorted(reasons),
+                "samples": len(rows), "power_w_max": max(float(r[4]) for r in rows)}
 
     def stop(self) -> dict:
         if self.p is None:
@@ -82,27 +99,26 @@ class ClockSampler:
         self.f.flush()
         rows = [r.split(", ") for r in Path(self.f.name).read_text().splitlines() if r.count(",") >= 9]
         os.unlink(self.f.name)
-        samples, all_rows = [], []
+        stamped = []
         for r in rows:
             try:
                 ts = time.mktime(time.strptime(r[0].split(".")[0], "%Y/%m/%d %H:%M:%S")) + float("0." + r[0].split(".")[1])
             except Exception:
                 continue
-            all_rows.append(r)
-            if self.t0 is not None and self.t0 - 0.06 <= ts <= (self.t1 or ts) + 0.06:
-                samples.append(r)
-        use = samples or all_rows[-3:]
-        if not use:
+            stamped.append((ts, r))
+        if not stamped:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[2]) for r in use]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in use:
-            for n, v in zip(names, r[6:10]):
-                if v.strip() == "Active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(use[0][3]), "reasons": sorted(reasons),
-                "samples": len(samples), "power_w_max": max(float(r[4]) for r in use)}
+        per_phase, inside = {}, []
+        for name, t0, t1 in self.phases:
+            sel = [r for ts, r in stamped if t0 - 0.06 <= ts <= (t1 or ts) + 0.06]
+            if sel:
+                per_phase.setdefault(name, []).extend(sel)
+                inside.extend(sel)
+        out = self._summary(inside or [r for _, r in stamped])
+        out["scope"] = "samples inside the measured phases" if inside else "all samples (no phase overlapped one)"
+        out["phases"] = {k: {kk: v for kk, v in self._summary(rs).items() if kk in ("sm_mhz", "reasons", "samples")}
+                         for k, rs in per_phase.items()}
+        return out
 
 
 def reference_block(cfg, seed, threads):
@@ -141,6 +157,65 @@ def time_reference(cfg, seed, sample_tokens, steps, warmup, threads, budget_s=No
                       f"{threads} OpenMP threads, experts in RAM"}
 
 
+def host_cpu() -> dict:
+    """CPU model, physical cores and logical CPUs of this host (the reference's OpenMP threads use all logical
+    CPUs)."""
+    model = None
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    phys = None
+    try:
+        import psutil
+        phys = psutil.cpu_count(logical=False)
+    except Exception:
+        pass
+    return {"cpu_model": model, "physical_cores": phys, "logical_cpus": os.cpu_count()}
+
+
+def time_reference_mode_r(cfg, seed, sample_tokens, threads, budget_s=8.0):
+    """The reference's UNMODIFIED moe_layer_step (Mode R): a synthetic checkpoint of the block (8-bit quantized
+    router, as real checkpoints have) is written in the MLX safetensors layout to a temporary directory, opened
+    with the reference's own k3_st_open / expert_tensor_open / load_qmat, and every token preads its 8 selected
+    experts from that page-cache-warm file (engine/src/expert_store.c:54-61), as the engine does."""
+    import shutil
+    import oracle as O
+    from oracle.checkpoint import checkpoint_tensors, write_safetensors
+    if not O.ref_available():
+        return None
+    bc = O.BlockCfg(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size, True)
+    blk = O.SynthBlock(bc, seed)
+    d = Path(tempfile.mkdtemp(prefix="qe_moder_"))
+    try:
+        prefix = "language_model.model.layers.0.mlp"
+        write_safetensors(d / "model.safetensors", checkpoint_tensors(prefix, blk.arrays()))
+        R = O.ref()
+        R.ref_set_threads(threads)
+        h = R.ref_r_open(str(d).encode(), prefix.encode(), cfg.hidden, cfg.top_k, cfg.inter, cfg.sh_inter,
+                         cfg.group_size)
+        if not h:
+            return None
+        x = blk.x(sample_tokens)
+        out = np.empty(cfg.hidden, np.float32)
+        for t in range(min(2, sample_tokens)):   # warm: the file is in the page cache after its first reads
+            R.ref_r_step(h, O.fptr(np.ascontiguousarray(x[t])), O.fptr(out))
+        done, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s:
+            R.ref_r_step(h, O.fptr(np.ascontiguousarray(x[done % sample_tokens])), O.fptr(out))
+            done += 1
+        sec = time.perf_counter() - t0
+        return {"value": done / sec, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                "sample": f"{done} tokens of {cfg.name} (8-bit quantized router) through the reference's unmodified "
+                          f"moe_layer_step, experts pread from a page-cache-warm safetensors file, {threads} threads"}
+    finally:
+        blk.close()
+        shutil.rmtree(d, ignore_errors=True)
+
+
 def run_reference_arm(args, cfg):
     rank, _, world = dist_env()
     if rank != 0:
@@ -153,6 +228,7 @@ def run_reference_arm(args, cfg):
     if res is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libqref.so (reference build) is missing"}))
         return
+    res.update(host_cpu())
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * args.ref_tokens / res["value"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -282,6 +358,90 @@ def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, mode, np
                          if phase_ms["return"] else None}}
 
 
+def sub_record(cfg, device, stream, args, nblocks=4, steps=None, warmup=5):
+    """One configuration measured like the headline (1 GPU, CUDA-graph replay of one block's forward per step,
+    nblocks blocks with distinct weights rotated, inputs in HBM, CUDA events on the launching stream), with the
+    roofline of the whole step and of its dominant kernel: HBM bytes for decode batches, tensor flops for prefill.
+    Stage times come from an eager, untimed repeat of the same forwards (qe_profile_begin/end)."""
+    import torch
+    import qmoe
+    T = cfg.tokens
+    steps = steps or (200 if T <= 64 else 40)
+    blocks = [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size,
+                            max_tokens=T, device=device, seed=b + 1, block=b) for b in range(nblocks)]
+    gen = torch.Generator(device="cuda").manual_seed(17)
+    x = torch.randn(T, cfg.hidden, device="cuda", generator=gen, dtype=torch.float32)
+    out = torch.empty_like(x)
+    sptr = stream.cuda_stream
+    graphs = [b.graph(T, x.data_ptr(), out.data_ptr()) for b in blocks]
+    for i in range(max(warmup, 3)):
+        graphs[i % nblocks].launch(sptr)
+    torch.cuda.synchronize()
+    l0 = qmoe.kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        graphs[i % nblocks].launch(sptr)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    launches = qmoe.kernel_launches() - l0
+    ms = e0.elapsed_time(e1) / steps
+    qmoe.profile_begin(device)
+    for i in range(min(steps, 40)):
+        blocks[i % nblocks].forward_device(T, x.data_ptr(), out.data_ptr(), sptr)
+    torch.cuda.synchronize()
+    stage_ms, passes = qmoe.profile_end(device)
+    per_pass = {k: v / max(passes, 1) for k, v in stage_ms.items()}
+    idx, _ = blocks[0].route(x.cpu().numpy())
+    uniq = len(np.unique(idx))
+    for g in graphs:
+        g.close()
+    for b in blocks:
+        b.close()
+    value = T / (ms / 1e3)
+    top = max(("gateup", "down"), key=lambda k: per_pass[k])
+    kname = expert_kernel_name(cfg, top, T)
+    rec = {"config": cfg.name, "workload": cfg.note, "tokens_per_step": T, "value": value, "unit": "tokens/s",
+           "ms_per_step": ms, "steps": steps, "blocks_rotated": nblocks, "cuda_graph": True,
+           "gpu_launches": launches, "unique_experts": uniq,
+           "stage_ms_per_pass": {k: round(v, 5) for k, v in per_pass.items()}}
+    if T <= 64:   # decode batches: HBM-bound; compulsory bytes of the step and of the dominant kernel
+        peak, kind = hbm_peak()
+        step_bytes = (uniq * cfg.expert_bytes + cfg.shared_bytes + 4 * (cfg.E + 1) * cfg.hidden
+                      + 8 * T * cfg.hidden)
+        kb = stage_bytes(cfg, uniq, T)[top]
+        kms = per_pass[top]
+        rec["roofline"] = {"bound": "hbm", "unit": "GB/s", "peak": peak,
+                           "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured"
+                           else "fallback 6.65 TB/s",
+                           "step": {"algorithmic_bytes": step_bytes, "achieved": step_bytes / (ms / 1e3) / 1e9,
+                                    "frac": step_bytes / (ms / 1e3) / 1e9 / peak},
+                           "kernel": kname, "kernel_ms": kms, "algorithmic_bytes_per_launch": kb,
+                           "achieved": kb / (kms / 1e3) / 1e9, "frac": kb / (kms / 1e3) / 1e9 / peak}
+    else:         # prefill: tensor-bound; algorithmic flops (the 2-term activation split is not counted)
+        peak, kind = tensor_peak()
+        step_flops = T * cfg.flops_per_token()
+        npair = T * (cfg.top_k + 1)
+        kf = (4 if top == "gateup" else 2) * npair * cfg.inter * cfg.hidden
+        kms = per_pass[top]
+        rec["roofline"] = {"bound": "tensor", "unit": "TFLOP/s", "peak": peak, "peak_source": kind,
+                           "step": {"algorithmic_flops": step_flops, "achieved": step_flops / (ms / 1e3) / 1e12,
+                                    "frac": step_flops / (ms / 1e3) / 1e12 / peak},
+                           "kernel": kname, "kernel_ms": kms, "algorithmic_flops_per_launch": kf,
+                           "achieved": kf / (kms / 1e3) / 1e12, "frac": kf / (kms / 1e3) / 1e12 / peak}
+    return rec
+
+
+def tensor_peak():
+    """Dense bf16 tensor peak for a kernel timed inside a long step: the sustained figure of MEASURED_PEAKS.json,
+    else the profiling recipe's fallback."""
+    try:
+        p = json.loads(PEAKS_FILE.read_text())
+        return float(p["bf16_tflops_sustained"]), "measured (MEASURED_PEAKS.json bf16_tflops_sustained)"
+    except Exception:
+        return 1400.0, "fallback 1.4 PFLOP/s sustained"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -296,6 +456,8 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=16)
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub-records", action="store_true",
+                    help="config c2 on 1 GPU: skip the decode and compute-bound prefill sub-records")
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="1 GPU: replay each block's forward as a captured CUDA graph (qe_moe_graph_create; auto: "
                          "on) or launch its kernels one by one (off)")
@@ -303,7 +465,6 @@ def main():
                     help="N > 1: exchange through peer memory (p2p) or NCCL all_to_all (sharded)")
     args = ap.parse_args()
 
-    from qmoe.synth import CONFIGS
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         run_reference_arm(args, cfg)
@@ -396,25 +557,24 @@ def main():
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    for i in range(max(args.warmup, 3)):
-        step(i)
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(local)   # sampled from here to the end: warm-up, timed steps, e2e and sub-records
+    clocks.mark("warmup", True)
     for i in range(max(args.warmup, 3)):
         step(i)
     barrier()
+    clocks.mark("warmup", False)
     launches0 = qmoe.kernel_launches() + graph_launches[0]
     qmoe.profile_begin(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks.mark(True)
+    clocks.mark("timed", True)
     e0.record(stream)
     for i in range(args.steps):
         step(i)
     e1.record(stream)
     barrier()
-    clocks.mark(False)
+    clocks.mark("timed", False)
     launches = qmoe.kernel_launches() + graph_launches[0] - launches0
     stage_ms, passes = qmoe.profile_end(local)
-    clk = clocks.stop()
     if not ep and use_graph:   # graphs carry no stage events: profile the same forwards eagerly, untimed
         qmoe.profile_begin(local)
         for i in range(min(args.steps, 50)):
@@ -519,8 +679,10 @@ def main():
             torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
         return world * T * ke / float(te.item())
 
+    clocks.mark("e2e", True)
     e2e_sync_value = timed_e2e(e2e_step)
     e2e_value = timed_e2e(e2e_async_step, e2e_async_wait)
+    clocks.mark("e2e", False)
 
     peak, peak_kind = hbm_peak()
     peak_source = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s")
@@ -558,10 +720,9 @@ def main():
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": dict(workload_config(cfg, world, args.blocks, "rows and partial sums stored into peer memory by "
-                                           "the kernels" if args.ep_mode == "p2p" else "all_to_all over NCCL",
-                                           args.stack),
-                           cuda_graph=use_graph),
+            "config": workload_config(cfg, world, args.blocks, "rows and partial sums stored into peer memory by "
+                                      "the kernels" if args.ep_mode == "p2p" else "all_to_all over NCCL", args.stack),
+            "cuda_graph": use_graph,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * cfg.hidden,
                     "d2h_bytes_per_step": 4 * T * cfg.hidden, "steps": ke,
                     "timing": "host clock, max over ranks; consecutive steps pipelined: each step's pinned-host "
@@ -571,7 +732,7 @@ def main():
                     "sync_value": e2e_sync_value,
                     "sync_timing": "one step at a time: copy in, forward, copy out, wait"
                                    + (" (ExpertParallelMoe.forward)" if ep else " (qe_moe_forward)")},
-            "roofline": roofline, "gpu_launches": launches, "clocks": clk}
+            "roofline": roofline, "gpu_launches": launches}
     if args.stack:   # every token passes through all blocks of the stack: block-level throughput for reference
         line["block_tokens_per_s"] = value * args.blocks
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -579,7 +740,30 @@ def main():
         if cb and args.stack:   # one block timed; a token through the stack takes `blocks` such passes
             cb["value"] /= args.blocks
             cb["sample"] += f"; one block timed, value divided by the stack's {args.blocks} blocks"
+        if cb:
+            cb.update(host_cpu())
+            if not args.stack:
+                mr = time_reference_mode_r(cfg, 1, args.ref_tokens, os.cpu_count() or 1)
+                if mr:
+                    cb["mode_r"] = mr
         line["cpu_baseline"] = cb if cb else {"value": None, "unavailable": "oracle/_ref missing"}
+    if world == 1 and not args.stack and args.config == "c2" and not args.no_sub_records:
+        # the other headline measurements in the same run: decode (config 1 at one token, one config-5 block at 64
+        # tokens) and compute-bound prefill (config 3 at 4096 tokens); each on its own rotated blocks
+        for b in blocks:
+            b.close()
+        if use_graph:
+            for g in graphs:
+                g.close()
+            use_graph = False
+        blocks = []
+        line["sub_records"] = {}
+        for name, key in (("decode_c1", "c1"), ("decode_c5_block", "c5"), ("prefill_compute_c3", "c3_prefill")):
+            clocks.mark(name, True)
+            line["sub_records"][name] = sub_record(CONFIGS[key], local, stream, args)
+            clocks.mark(name, False)
+        line["gpu_launches"] += sum(r["gpu_launches"] for r in line["sub_records"].values())
+    line["clocks"] = clocks.stop()
     if ep:
         if use_graph:   # the captured steps reference the exchange buffers: drop them before those are freed
             torch.cuda.synchronize()

@@ -94,8 +94,11 @@ int qe_moe_forward(QeMoe *m, int T, const float *x, float *out);
  * out[T][hidden] back, and returns without waiting; qe_moe_forward_wait(m) waits for every such call on m's
  * device. Consecutive calls overlap their copies with each other's kernels (two staging slots per device; x
  * and out in pinned host memory for the copies to be asynchronous). x and out must stay valid and out unread
- * until the wait. Same results as qe_moe_forward; T <= max_tokens; the routing trace and the read statistics
- * are not updated. No reference counterpart (moe_layer_step returns with out written). 0 ok, -1 error. */
+ * until the wait. The forward is replayed from CUDA graphs that the handle's first call with a given T
+ * captures for both staging slots at once (that call synchronises the device; so does a call that grows the
+ * staging buffers); every later call with that T only enqueues work. Same results as qe_moe_forward;
+ * T <= max_tokens; the read statistics are not updated and the routing trace (QE_TRACE) is not written.
+ * No reference counterpart (moe_layer_step returns with out written). 0 ok, -1 error. */
 int qe_moe_forward_async(QeMoe *m, int T, const float *x, float *out);
 int qe_moe_forward_wait(QeMoe *m);
 
@@ -181,6 +184,9 @@ int qe_moe_ep_dispatch_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, const 
  * rank must make the same sequence of calls, each on its own GPU (ranks emulated on one GPU must not use it:
  * a wait on a kernel of the same GPU may never end). A timeout is reported by qe_device_error() (200 + 1). */
 int qe_ep_xchg_barrier(QeEpXchg *x, void *stream);
+/* Bound of each wait in this context's qe_ep_xchg_barrier calls, 1 ms .. 60 s (default 2 s); a barrier launched
+ * afterwards uses it (a CUDA graph keeps the bound it was captured with). 0 ok, -1 error. */
+int qe_ep_xchg_set_timeout_ms(QeEpXchg *x, int ms);
 int qe_moe_ep_route_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, int32_t *meta, void *stream);
 int qe_moe_ep_experts_p2p(QeMoe *m, QeEpXchg *xc, int T, void *stream);
 int qe_moe_ep_combine_p2p(QeMoe *m, QeEpXchg *xc, int T, const int32_t *home, const float *shared, float *out,
@@ -237,10 +243,17 @@ int qe_profile_begin(int device);
 int qe_profile_end(int device, double *stage_ms, int *passes);
 /* Kernels launched by this library since process start. */
 unsigned long long qe_kernel_launches(void);
+/* Forwards this library captured into CUDA graphs since process start (qe_moe_graph_create, and the graphs
+ * qe_moe_forward_async captures for both staging slots on a handle's first call with a batch size). */
+unsigned long long qe_graph_captures(void);
 /* Nonzero if a bounded wait on the device timed out (the kernel then returned early; outputs invalid): a
  * tensor-core kernel's pipeline wait (its code), the fused decode step's grid barrier (100 + code), or the
  * exchange barrier of qe_ep_xchg_barrier (201). */
 int qe_device_error(void);
+/* qe_device_error for `device` (the caller's current device is left as it was). */
+int qe_device_error_on(int device);
+/* Clear every recorded timeout code on `device` (after the caller handled one). 0 ok, -1 error. */
+int qe_device_error_reset(int device);
 
 #ifdef __cplusplus
 }

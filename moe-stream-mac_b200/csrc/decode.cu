@@ -483,3 +483,8 @@ int qe_decode_error(void) {
     if (cudaMemcpyFromSymbol(&v, g_decode_error, sizeof(int)) != cudaSuccess) return -1;
     return v;
 }
+
+int qe_decode_error_reset(void) {
+    const int zero = 0;
+    return cudaMemcpyToSymbol(g_decode_error, &zero, sizeof(int)) == cudaSuccess ? 0 : -1;
+}

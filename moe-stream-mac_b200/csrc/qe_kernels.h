@@ -74,6 +74,7 @@ int qe_launch_decode_fused(const QeExpertArgs *a, const float *W, const float *b
                            float *logits, int32_t *idx, float *score, float *h3, int ldh, float *out, unsigned *bar,
                            int sms, cudaStream_t s);
 int qe_decode_error(void);
+int qe_decode_error_reset(void);
 /* Expert-centric grouped GEMVs for batched decode (group_gemv.cu). */
 bool qe_group_supported(const QeExpertArgs *a);
 int qe_group_tokens(void);
@@ -119,6 +120,7 @@ int qe_launch_tc_gateup(const QeExpertArgs *a, const void *maps, const float *x,
 int qe_launch_tc_down(const QeExpertArgs *a, const void *maps, const QeBuckets *b, int T, int tn, const QeTcBufs *t,
                       float *ybuf, int grid, cudaStream_t s);
 int qe_tc_error(void);
+int qe_tc_error_reset(void);
 int qe_tc_bm(void);
 int qe_tc_tokens_per_tile(int T, int top_k, int E);
 

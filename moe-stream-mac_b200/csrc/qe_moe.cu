@@ -58,6 +58,7 @@ DevCtx g_dev[64];
 std::atomic<unsigned long long> g_bytes_read{0};
 double g_gpu_seconds = 0.0;
 std::atomic<unsigned long long> g_launches{0};
+std::atomic<unsigned long long> g_captures{0};   /* forwards captured into CUDA graphs */
 
 /* Stage profiling: when enabled, every pass records one event before the router and one after each of
  * the QE_STAGES stages on the stream it runs on; qe_profile_end sums the per-stage elapsed times. */
@@ -959,6 +960,7 @@ QeMoeGraph *qe_moe_graph_create(QeMoe *m, int T, const float *x, float *out) {
     }
     g->device = m->device;
     g->launches = g_launches.load() - l0;
+    g_captures += 1;
     return g;
 }
 
@@ -1015,17 +1017,23 @@ int qe_moe_forward_async(QeMoe *m, int T, const float *x, float *out) {
     scratch_layout(m->cfg, T, (char *)d->ws, &sc);
     const int j = (int)(d->async_n++ & 1);
     float *xd = d->stage + (size_t)(2 * j) * d->stage_cap, *od = xd + d->stage_cap;
-    /* the forward replayed from a CUDA graph captured for this slot and T (no per-kernel launch gaps): captured
-     * on first use, with the device idle, since the capture runs an eager forward on the slot's buffers */
+    /* The forward is replayed from a CUDA graph captured for this handle, staging slot and T (no per-kernel launch
+     * gaps). The graphs of BOTH slots are captured together, on the handle's first call with this T (or after the
+     * staging buffers grew), with the device idle, since each capture runs an eager forward on the slot's
+     * buffers; later calls with the same T never capture, whichever slot they get. */
     static const bool use_graph = !getenv("QE_ASYNC_GRAPH") || strcmp(getenv("QE_ASYNC_GRAPH"), "0") != 0;
     if (use_graph && !(m->agraph[j] && m->a_T[j] == T && m->a_x[j] == xd && m->a_o[j] == od)) {
         QE_CHECK(cudaDeviceSynchronize());
-        qe_moe_graph_free(m->agraph[j]);
-        m->agraph[j] = qe_moe_graph_create(m, T, xd, od);
-        if (!m->agraph[j]) QE_FAIL("forward_async: graph capture failed");
-        m->a_T[j] = T;
-        m->a_x[j] = xd;
-        m->a_o[j] = od;
+        for (int q = 0; q < 2; q++) {
+            float *xq = d->stage + (size_t)(2 * q) * d->stage_cap, *oq = xq + d->stage_cap;
+            if (m->agraph[q] && m->a_T[q] == T && m->a_x[q] == xq && m->a_o[q] == oq) continue;
+            qe_moe_graph_free(m->agraph[q]);
+            m->agraph[q] = qe_moe_graph_create(m, T, xq, oq);
+            if (!m->agraph[q]) QE_FAIL("forward_async: graph capture failed");
+            m->a_T[q] = T;
+            m->a_x[q] = xq;
+            m->a_o[q] = oq;
+        }
     }
     if (d->slot_used[j]) QE_CHECK(cudaStreamWaitEvent(d->s_in, d->ev_comp[j], 0));
     QE_CHECK(cudaMemcpyAsync(xd, x, sizeof(float) * nf, cudaMemcpyHostToDevice, d->s_in));
@@ -1214,6 +1222,7 @@ struct QeEpXchg {
     bool opened[64];
     void **dptr;                     /* device arrays: recv_x[G], recv_meta[G], back[G]                          */
     int T;                           /* tokens per rank of the current step                                     */
+    unsigned long long wait_ns;      /* bound of each wait in qe_ep_xchg_barrier (qe_ep_xchg_set_timeout_ms)    */
 };
 
 namespace {
@@ -1357,7 +1366,7 @@ int qe_ep_xchg_barrier(QeEpXchg *x, void *stream) {
     if (x->G > 32) QE_FAIL("ep_xchg_barrier: %d ranks (one warp serves at most 32)", x->G);
     QE_CHECK(cudaSetDevice(x->m->device));
     ep_barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((unsigned *const *)(x->dptr + 3 * x->G), x->self, x->G,
-                                                         2000000000ull);
+                                                         x->wait_ns ? x->wait_ns : 2000000000ull);
     QE_CHECK(cudaGetLastError());
     g_launches += 1;
     return 0;
@@ -1570,12 +1579,38 @@ int qe_profile_end(int device, double *stage_ms, int *passes) {
 }
 
 unsigned long long qe_kernel_launches(void) { return g_launches.load(); }
+unsigned long long qe_graph_captures(void) { return g_captures.load(); }
 
 int qe_device_error(void) {
     const int t = qe_tc_error(), d = qe_decode_error();
     int e = 0;
     if (cudaMemcpyFromSymbol(&e, g_ep_error, sizeof(int)) != cudaSuccess) return -1;
     return t ? t : d ? 100 + d : e ? 200 + e : 0;
+}
+
+int qe_device_error_on(int device) {
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess || cudaSetDevice(device) != cudaSuccess) return -1;
+    const int e = qe_device_error();
+    cudaSetDevice(cur);
+    return e;
+}
+
+int qe_device_error_reset(int device) {
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) return -1;
+    QE_CHECK(cudaSetDevice(device));
+    const int zero = 0;
+    const int rc = qe_tc_error_reset() || qe_decode_error_reset() ||
+                   cudaMemcpyToSymbol(g_ep_error, &zero, sizeof(int)) != cudaSuccess;
+    cudaSetDevice(cur);
+    return rc ? -1 : 0;
+}
+
+int qe_ep_xchg_set_timeout_ms(QeEpXchg *x, int ms) {
+    if (!x || ms < 1 || ms > 60000) QE_FAIL("ep_xchg_set_timeout_ms: bad arguments");
+    x->wait_ns = (unsigned long long)ms * 1000000ull;
+    return 0;
 }
 
 double qe_expert_gb_read(void) { return (double)g_bytes_read.load() / 1e9; }

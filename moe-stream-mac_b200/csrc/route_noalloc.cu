@@ -14,6 +14,8 @@
  * the address up with cudaGetSymbolAddress (with that device current) and caches it, so that first call
  * should come before any stream capture.
  */
+#include <atomic>
+
 #include "qe_common.cuh"
 #include "qe_kernels.h"
 #include "../../include/qe_moe.h"
@@ -22,7 +24,9 @@
 
 static __device__ __align__(256) float qe_noalloc_logits[QE_NOALLOC_LOGITS];
 
-static float *g_noalloc_logits[64]; /* device address of qe_noalloc_logits, per device */
+/* device address of qe_noalloc_logits, per device; atomic, since two host threads may make their first calls on a
+ * device at the same time (both then store the same address) */
+static std::atomic<float *> g_noalloc_logits[64];
 
 extern "C" int qe_route_f32_noalloc(const float *router_w, const float *router_bias, const float *x, int T, int hidden,
                                     int E, int top_k, int32_t *idx, float *score, void *stream) {
@@ -36,14 +40,15 @@ extern "C" int qe_route_f32_noalloc(const float *router_w, const float *router_b
     int dev = 0;
     QE_CHECK(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) QE_FAIL("route_noalloc: device %d out of range", dev);
-    if (!g_noalloc_logits[dev]) {
+    float *logits = g_noalloc_logits[dev].load(std::memory_order_acquire);
+    if (!logits) {
         void *p = nullptr;
         QE_CHECK(cudaGetSymbolAddress(&p, qe_noalloc_logits));
-        g_noalloc_logits[dev] = static_cast<float *>(p);
+        logits = static_cast<float *>(p);
+        g_noalloc_logits[dev].store(logits, std::memory_order_release);
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (qe_launch_router_f32(router_w, router_bias, x, T, hidden, E, g_noalloc_logits[dev], nullptr, nullptr, nullptr,
-                             s) < 0)
+    if (qe_launch_router_f32(router_w, router_bias, x, T, hidden, E, logits, nullptr, nullptr, nullptr, s) < 0)
         return -1;
-    return qe_launch_route_topk(g_noalloc_logits[dev], E + 1, T, E, top_k, idx, score, nullptr, s);
+    return qe_launch_route_topk(logits, E + 1, T, E, top_k, idx, score, nullptr, s);
 }

@@ -7,7 +7,7 @@ and loading fails loudly if libqengine_b200.so is missing.
 """
 from .lib import (QeMoeConfig, QeMoeWeights, QeQTensor, QE_ROUTER_F32, QE_ROUTER_QMAT, LIB_PATH, build, lib,
                   qmat_matvec, route_logits, op_silu_mul, op_sigmoid, op_expf, expert_gb_read,
-                  expert_read_seconds, device_count, profile_begin, profile_end, kernel_launches,
+                  expert_read_seconds, device_count, profile_begin, profile_end, kernel_launches, graph_captures,
                   STAGES, safetensors_tensor_info)
 from .block import MoeBlock, EngineError
 from .synth import CONFIGS, MoeConfig, zipf_router_bias
@@ -15,5 +15,5 @@ from .synth import CONFIGS, MoeConfig, zipf_router_bias
 __all__ = ["QeMoeConfig", "QeMoeWeights", "QeQTensor", "QE_ROUTER_F32", "QE_ROUTER_QMAT", "LIB_PATH", "build", "lib",
            "qmat_matvec", "route_logits", "op_silu_mul", "op_sigmoid", "op_expf", "expert_gb_read",
            "expert_read_seconds", "device_count", "profile_begin", "profile_end",
-           "kernel_launches", "STAGES", "MoeBlock", "EngineError", "CONFIGS", "MoeConfig",
+           "kernel_launches", "graph_captures", "STAGES", "MoeBlock", "EngineError", "CONFIGS", "MoeConfig",
            "zipf_router_bias", "safetensors_tensor_info"]

@@ -69,7 +69,11 @@ def lib() -> C.CDLL:
         L.qe_profile_begin.argtypes = [C.c_int]
         L.qe_profile_end.argtypes = [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         L.qe_kernel_launches.restype = C.c_ulonglong
+        L.qe_graph_captures.restype = C.c_ulonglong
         L.qe_device_error.restype = C.c_int
+        L.qe_device_error_on.argtypes = [C.c_int]
+        L.qe_device_error_reset.argtypes = [C.c_int]
+        L.qe_ep_xchg_set_timeout_ms.argtypes = [vp, C.c_int]
         L.qe_route_f32_noalloc.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp]
         L.qe_moe_ep_route_device.argtypes = [vp, C.c_int, vp, vp, vp, vp]
         L.qe_moe_forward_async.argtypes = [vp, C.c_int, vp, vp]
@@ -179,6 +183,11 @@ def profile_end(device: int = 0) -> tuple[dict, int]:
 
 def kernel_launches() -> int:
     return lib().qe_kernel_launches()
+
+
+def graph_captures() -> int:
+    """Forwards the library has captured into CUDA graphs since the process started."""
+    return lib().qe_graph_captures()
 
 
 def device_count() -> int:

@@ -251,3 +251,32 @@ def test_ep_nccl_two_gpus(mode):
         rank, rel, err = q.get(timeout=10)
         assert err == 0, (rank, err)
         assert rel <= 5e-6, (rank, rel)
+
+
+def test_exchange_barrier_timeout_is_reported_and_cleared():
+    """qe_ep_xchg_barrier's bounded wait: with two contexts of one GPU connected and only one of them entering
+    the barrier (the other's flag is never written), the wait gives up after the 20 ms bound set here, the kernel
+    returns, qe_device_error_on reports 201 for that device, and qe_device_error_reset clears it. No kernel waits
+    on another kernel: the peer never launches anything."""
+    import ctypes as C
+    from qmoe.ep import DeviceEngine
+    from qmoe.lib import lib
+    cfg = dict(hidden=256, E=16, top_k=4, inter=128, sh_inter=128, bits=4)
+    blocks = [qmoe.MoeBlock(**cfg, seed=3, ep_rank=r, ep_size=2, max_tokens=16) for r in range(2)]
+    eng = [DeviceEngine(b) for b in blocks]
+    for e in eng:
+        e.xchg_create(16)
+    arr = (C.c_void_p * 2)(*[e.xchg for e in eng])
+    assert lib().qe_ep_xchg_connect_local(arr, 2) == 0
+    assert lib().qe_device_error_reset(0) == 0
+    assert lib().qe_ep_xchg_set_timeout_ms(C.c_void_p(eng[0].xchg), 20) == 0
+    assert lib().qe_ep_xchg_set_timeout_ms(C.c_void_p(eng[0].xchg), 0) == -1
+    eng[0].xchg_barrier()
+    torch.cuda.synchronize()
+    assert lib().qe_device_error_on(0) == 201
+    assert lib().qe_device_error_reset(0) == 0
+    assert lib().qe_device_error_on(0) == 0
+    for e in eng:
+        e.xchg_free()
+    for b in blocks:
+        b.close()

@@ -121,13 +121,19 @@ class ClockSampler:
         return out
 
 
+def router_bias(cfg, seed):
+    """The configuration's skewed-popularity router bias (Zipf law over a seeded permutation), or None."""
+    from qmoe.synth import zipf_router_bias
+    return zipf_router_bias(cfg.E, cfg.zipf_s, seed=seed) if cfg.zipf_s else None
+
+
 def reference_block(cfg, seed, threads):
     import oracle as O
     if not O.ref_available():
         return None, None
     O.ref().ref_set_threads(threads)
     blk = O.SynthBlock(O.BlockCfg(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size),
-                       seed)
+                       seed, router_bias=router_bias(cfg, seed))
     return O, blk
 
 
@@ -249,7 +255,9 @@ def workload_config(cfg, world, blocks=4, ep_mode="rows and partial sums stored 
             "group_size": cfg.group_size, "router": "fp32", "parallelism": "1 GPU" if world == 1 else
             f"expert parallel over {world} GPUs ({cfg.E // world} experts each; router and shared expert "
             f"replicated; {cfg.tokens} tokens per GPU; exchange: {ep_mode})",
-            "l2": l2, "stack_blocks": blocks if stack else None}
+            "l2": l2, "stack_blocks": blocks if stack else None,
+            "routing": (f"router logit bias -{0.75 * cfg.zipf_s:g} ln(popularity rank) (Zipf({cfg.zipf_s:g})-skewed)"
+                        if cfg.zipf_s else "seeded random router, no bias")}
 
 
 def profiled_traffic(kernel: str, config: str):
@@ -307,11 +315,13 @@ def stage_bytes(cfg, uniq: int, T: int) -> dict:
     return {"gateup": gu, "down": dn}
 
 
-def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, mode, nprof=10):
+def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, mode, placement=None, spare=0, nprof=10):
     """Per-phase times of the expert-parallel step (CUDA events between phases, a separate run after the
     timed region) and the roofline of its expert stage: this rank's touched experts' weights once, plus the
-    rows it receives and the partial sums it returns."""
+    rows it receives and the partial sums it returns. With the assignments every rank serves under the
+    placement used and under contiguous ranges (the busiest rank sets the step's time)."""
     import torch
+    from qmoe.placement import Placement
     names = ("route", "pack", "dispatch", "experts", "return", "combine")
     acc = dict.fromkeys(names, 0.0)
     for i in range(nprof):
@@ -334,10 +344,13 @@ def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, mode, np
     idx, _ = models[0].engine.block.route(x.cpu().numpy())
     allidx = torch.empty(world * idx.size, dtype=torch.int32, device="cuda")
     torch.distributed.all_gather_into_tensor(allidx, torch.from_numpy(idx.reshape(-1)).cuda())
-    El = cfg.E // world
     ids = allidx.cpu().numpy().reshape(-1, cfg.top_k)
-    local = (ids >= rank * El) & (ids < (rank + 1) * El)
+    by_src = ids.reshape(world, -1, cfg.top_k)
+    used = placement or Placement.contiguous(cfg.E, world)
+    local = np.concatenate([used.dest(by_src[s], s) for s in range(world)]) == rank
     uniq = len(np.unique(ids[local]))
+    loads = used.rank_loads(by_src)
+    plain = Placement.contiguous(cfg.E, world).rank_loads(by_src)
     rows, pairs = int(local.any(axis=1).sum()), int(local.sum())   # rows received, (row, expert) pairs
     H, I = cfg.hidden, cfg.inter
     # weights of the touched experts once; x rows in, partial rows out; h3 written and read; y per pair
@@ -351,6 +364,12 @@ def ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, mode, np
     return {"bound": "hbm", "kernel": f"expert stage (qe_moe_ep_experts_{'p2p' if mode == 'p2p' else 'device'}) on rank {rank}", "achieved": achieved,
             "peak": peak, "unit": "GB/s", "frac": achieved / peak, "traffic": None, "peak_source": peak_source,
             "algorithmic_bytes_per_launch": nbytes, "unique_local_experts": uniq,
+            "rank_assignments": {"placement": "planned" if placement is not None else "contiguous",
+                                 "spare_slots_per_rank": spare,
+                                 "replicated_experts": int((used.nrep > 1).sum()),
+                                 "per_rank": loads.tolist(), "max_over_mean": float(loads.max() / loads.mean()),
+                                 "contiguous_per_rank": plain.tolist(),
+                                 "contiguous_max_over_mean": float(plain.max() / plain.mean())},
             "phase_ms": {k: round(v, 5) for k, v in phase_ms.items()},
             "exchange": {"bytes_sent_per_rank_each_way": xbytes,
                          "dispatch_GBs": xbytes / (phase_ms["dispatch"] / 1e3) / 1e9 if phase_ms["dispatch"] else None,
@@ -463,6 +482,12 @@ def main():
                          "on) or launch its kernels one by one (off)")
     ap.add_argument("--ep-mode", default="p2p", choices=["p2p", "sharded"],
                     help="N > 1: exchange through peer memory (p2p) or NCCL all_to_all (sharded)")
+    ap.add_argument("--placement", default="auto", choices=["auto", "contiguous", "planned"],
+                    help="N > 1: experts in contiguous ranges per rank, or a placement planned from a calibration "
+                         "batch's routing with hot experts replicated into spare slots (auto: planned when the "
+                         "configuration's routing is skewed)")
+    ap.add_argument("--spare-slots", type=int, default=-1,
+                    help="planned placement: replica slots per rank beyond E/N (default E/N/8, at least 1)")
     args = ap.parse_args()
 
     cfg = CONFIGS[args.config]
@@ -491,7 +516,19 @@ def main():
     graph_launches = [0]   # kernels launched by replays of torch-captured graphs (not seen by the library)
     if ep:
         from qmoe.ep import ExpertParallelMoe
-        models = [ExpertParallelMoe.on_gpu(cfg, rank, world, local, seed=b + 1, block=b, max_tokens=(world + 1) * T)
+        planned = args.placement == "planned" or (args.placement == "auto" and cfg.zipf_s > 0)
+        spare = args.spare_slots if args.spare_slots >= 0 else max(1, cfg.E // world // 8)
+        placements = []
+        for b in range(args.blocks):
+            if planned:   # calibration tokens: a batch distinct from the timed one, on every rank
+                xc = torch.randn(T, cfg.hidden, device="cuda", generator=torch.Generator(device="cuda").manual_seed(
+                    1000 + 7 * b + rank))
+                placements.append(ExpertParallelMoe.plan_placement(cfg, rank, world, local, xc, spare, seed=b + 1,
+                                                                   block=b, router_bias=router_bias(cfg, b + 1)))
+            else:
+                placements.append(None)
+        models = [ExpertParallelMoe.on_gpu(cfg, rank, world, local, seed=b + 1, block=b, max_tokens=(world + 1) * T,
+                                           router_bias=router_bias(cfg, b + 1), placement=placements[b])
                   for b in range(args.blocks)]
         if args.ep_mode == "p2p":
             for mdl in models:
@@ -531,7 +568,8 @@ def main():
                     graph_launches[0] += n
     else:
         blocks = [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, cfg.group_size,
-                                max_tokens=T, device=local, seed=b + 1, block=b) for b in range(args.blocks)]
+                                max_tokens=T, device=local, seed=b + 1, block=b, router_bias=router_bias(cfg, b + 1))
+                  for b in range(args.blocks)]
 
         def step(i):
             if args.stack:
@@ -687,7 +725,8 @@ def main():
     peak, peak_kind = hbm_peak()
     peak_source = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s")
     if ep:
-        roofline = ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, args.ep_mode)
+        roofline = ep_roofline(cfg, models, x, stream, rank, world, peak, peak_source, args.ep_mode, placements[0],
+                               spare if planned else 0)
     else:
         # roofline of the dominant kernel (per-stage CUDA events recorded inside the timed region)
         idx, _ = blocks[0].route(x.cpu().numpy())
@@ -733,6 +772,10 @@ def main():
                     "sync_timing": "one step at a time: copy in, forward, copy out, wait"
                                    + (" (ExpertParallelMoe.forward)" if ep else " (qe_moe_forward)")},
             "roofline": roofline, "gpu_launches": launches}
+    if ep:
+        line["config"]["placement"] = (f"planned per block from a calibration batch's routing (qmoe.placement): "
+                                       f"{cfg.E // world + spare} expert slots per rank, hot experts replicated"
+                                       if planned else f"contiguous: {cfg.E // world} experts per rank")
     if args.stack:   # every token passes through all blocks of the stack: block-level throughput for reference
         line["block_tokens_per_s"] = value * args.blocks
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

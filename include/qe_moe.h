@@ -41,8 +41,22 @@ typedef struct {
     int layer;            /* layer id written to the QE_TRACE routing trace (moe_layer.c:57-64) */
     int ep_rank, ep_size; /* expert parallelism: this handle holds routed experts [ep_rank*E/ep_size,
                              (ep_rank+1)*E/ep_size) plus the router and the shared expert (replicated).
-                             ep_size 0 or 1 = all experts (then ep_rank must be 0). ep_size must divide E. */
+                             ep_size 0 or 1 = all experts (then ep_rank must be 0). ep_size must divide E
+                             unless a placement is given. */
+    const int32_t *placement; /* NULL: the contiguous ranges above. Else a host table [ep_size][slots], the
+                             same on every rank: row r lists the global expert ids rank r holds (-1 = empty
+                             slot; no id twice in a row; every id in at least one row). An expert held by
+                             n > 1 ranks (a replicated hot expert) serves each token on one of them, chosen
+                             by the rule under QE_EP_ROUTED below. Needs ep_size > 1. Copied at create. */
+    int slots;            /* columns of placement */
 } QeMoeConfig;
+
+/* Expert placement: a (token, expert) assignment goes to rank reps[e][(t + src) % nrep[e]], where reps[e]
+ * lists the nrep[e] ranks holding e in ascending order, t is the token's row on its source rank and src is
+ * that rank (0 in the replicated step, where every rank holds the same rows). In the slot lists that
+ * qe_moe_ep_pack_device / qe_moe_ep_dispatch_p2p write for destination d, the ids of the slots routed to d
+ * carry QE_EP_ROUTED and the other slots are -1. */
+#define QE_EP_ROUTED 0x40000000
 
 /* One quantized tensor in the MLX affine layout (engine/include/qmat.h:3-11): uint32 codes
  * [n][rows][cols*bits/32] (LSB first), bf16 scales and biases [n][rows][cols/group_size]. */
@@ -121,18 +135,20 @@ int qe_moe_route(QeMoe *m, int T, const float *x, int32_t *idx, float *score);
 
 /* ---- expert parallelism (one process and one handle per GPU; the caller runs the collectives) ----
  * No counterpart in the reference (single-process, engine/src/moe_layer.c). Experts are sharded by id:
- * expert e lives on rank e / (E/ep_size). All buffers are device buffers on the handle's device, enqueued
- * on `stream` (a cudaStream_t). A token's slot list "meta" is int32 [2*top_k]: the k global expert ids
- * (-1 = empty slot) followed by the k renormalised scores' float bits.
+ * expert e lives on rank e / (E/ep_size), or where cfg.placement puts it. All buffers are device buffers on
+ * the handle's device, enqueued on `stream` (a cudaStream_t). A token's slot list "meta" is int32 [2*top_k]:
+ * the k global expert ids (-1 = empty slot) followed by the k renormalised scores' float bits.
  *
  * Token-sharded step (prefill batches, C4/C5 style), per rank with its own T tokens, G = ep_size:
  *   qe_moe_ep_route_device    route x, write meta[T][2k], and the gated shared-expert term shared[T][h]
- *   qe_moe_ep_pack_device     send_x[G][T][h], send_meta[G][T][2k]: rows of the tokens with >= 1 expert on
- *                             rank d go to block d in token order, the rest of the block is padding (meta ids
+ *   qe_moe_ep_pack_device     send_x[G][T][h], send_meta[G][T][2k]: rows of the tokens with >= 1 slot routed
+ *                             to rank d go to block d in token order (ids of the slots routed elsewhere -1,
+ *                             the others tagged QE_EP_ROUTED), the rest of the block is padding (meta ids
  *                             -1); home[G][T] = a token's row in block d or -1; counts[G] rows per block
  *   (caller) all_to_all of send_x and send_meta in equal blocks of T rows
- *   qe_moe_ep_experts_device  partial[n][h] for received rows: sum over the slots this rank owns, in slot
- *                             order, of score * expert(x)  (rows without such slots give 0)
+ *   qe_moe_ep_experts_device  partial[n][h] for received rows: sum over the slots routed to this rank, in
+ *                             slot order, of score * expert(x)  (rows without such slots give 0); untagged
+ *                             ids (the replicated step's own meta) count where their replica is this rank
  *   (caller) all_to_all of partial back to the home ranks
  *   qe_moe_ep_combine_device  out[t] = (sum over d ascending of part[d][home[d][t]]) + shared[t]
  * Replicated step (decode: every rank holds the same T tokens): route, experts on the own meta, an all-gather
@@ -146,6 +162,8 @@ int qe_moe_ep_experts_device(QeMoe *m, int n, const float *x, const int32_t *met
 int qe_moe_ep_combine_device(QeMoe *m, int T, const float *part, const int32_t *home, const float *shared, float *out,
                              void *stream);
 int qe_moe_ep_size(const QeMoe *m);
+/* Number of routed experts this handle holds; their global ids in slot order into ids (may be NULL). */
+int qe_moe_ep_experts(const QeMoe *m, int32_t *ids);
 
 /* Token-sharded step with the exchange done by the kernels themselves through peer memory (NVLink stores
  * into CUDA-IPC mappings of the other ranks' buffers), instead of two all_to_all calls:
@@ -233,6 +251,14 @@ int qe_route_f32_noalloc(const float *router_w, const float *router_bias, const 
 double qe_expert_gb_read(void);        /* GB of expert weights streamed from HBM by qe_moe_forward */
 double qe_expert_read_seconds(void);   /* GPU seconds spent in qe_moe_forward's kernels            */
 int qe_device_count(void);
+/* Host threads the library uses from now on for its CPU-side work: paging a checkpoint's (or a host weight
+ * array's) expert bytes in, in parallel, before they are copied to HBM (the GPU does the math). n <= 0 keeps
+ * the current count. Returns the effective count (default: the host's hardware threads). Same signature and
+ * return convention as the reference's qe_set_threads (engine/src/qengine.c:35-43, OpenMP threads there). */
+int qe_set_threads(int n);
+/* Peak resident set size of the process in GiB (getrusage; engine/src/qengine.c:47). Linux reports ru_maxrss
+ * in KiB, macOS (the reference's platform) in bytes: the value here is converted from KiB. */
+double qe_peak_rss_gb(void);
 
 /* ---- profiling (no reference counterpart: the reference times only its expert reads, moe_layer.c:74-78) ---- */
 enum { QE_STAGE_ROUTER = 0, QE_STAGE_TOPK, QE_STAGE_BUCKET, QE_STAGE_GATEUP, QE_STAGE_DOWN, QE_STAGE_COMBINE,

@@ -16,7 +16,9 @@
 #include <time.h>
 #include <atomic>
 #include <mutex>
+#include <thread>
 #include <vector>
+#include <sys/resource.h>
 
 #include "qe_common.cuh"
 #include "qe_kernels.h"
@@ -56,6 +58,39 @@ struct DevCtx {
 std::mutex g_mu;
 DevCtx g_dev[64];
 std::atomic<unsigned long long> g_bytes_read{0};
+std::atomic<int> g_host_threads{0};   /* qe_set_threads; 0 = the host's hardware threads */
+
+int host_threads() {
+    const int n = g_host_threads.load();
+    if (n > 0) return n;
+    const unsigned hw = std::thread::hardware_concurrency();
+    return hw ? (int)hw : 1;
+}
+
+/* Touch one byte per 4 KiB page of [p, p + bytes) on the library's host threads, so that a memory-mapped
+ * checkpoint is read from the file in parallel before the (single-threaded) copy to HBM walks it. */
+void page_in(const void *p, size_t bytes) {
+    constexpr size_t kPage = 4096, kMinPerThread = 8u << 20;
+    const int nt = (int)std::min<size_t>((size_t)host_threads(), std::max<size_t>(1, bytes / kMinPerThread));
+    const char *c = (const char *)p;
+    auto touch = [c](size_t a, size_t b) {
+        unsigned sum = 0;
+        for (size_t o = a; o < b; o += kPage) sum += (unsigned char)((const volatile char *)c)[o];
+        if (b > a) sum += (unsigned char)((const volatile char *)c)[b - 1];
+        (void)sum;
+    };
+    if (nt <= 1) {
+        touch(0, bytes);
+        return;
+    }
+    std::vector<std::thread> pool;
+    const size_t per = (bytes / nt + kPage - 1) / kPage * kPage;
+    for (int i = 0; i < nt; i++) {
+        const size_t a = std::min(bytes, (size_t)i * per), b = std::min(bytes, a + per);
+        if (a < b) pool.emplace_back(touch, a, b);
+    }
+    for (auto &t : pool) t.join();
+}
 double g_gpu_seconds = 0.0;
 std::atomic<unsigned long long> g_launches{0};
 std::atomic<unsigned long long> g_captures{0};   /* forwards captured into CUDA graphs */
@@ -186,7 +221,11 @@ struct QeMoe {
     QeQDev router_q, sh_router_q;
     QeExpertArgs ex;
     size_t expert_bytes;    /* bytes of one routed expert (gate+up+down codes, scales, biases) */
-    int e0, E_loc;          /* routed experts held here: global ids [e0, e0 + E_loc) (expert parallelism) */
+    int e0, E_loc;          /* routed experts held here: E_loc of them, global ids held[0 .. E_loc) in slot order
+                             * ([e0, e0 + E_loc) without a placement table; e0 = -1 with one) */
+    int32_t held[512];
+    int32_t *place;         /* device [E][2 + ep_size]: local slot of e here (-1: not held), replica count, the
+                             * holding ranks ascending (expert parallelism) */
     int path;               /* 0 = auto, 1 = mma.sync, 2 = tensor-core (tcgen05), 3 = decode GEMVs, 4 = grouped GEMVs */
     bool tc;                /* tensor-core path available for this shape */
     bool decode;            /* decode GEMVs available for this shape */
@@ -218,10 +257,54 @@ int validate(const QeMoeConfig *c) {
     if (c->router_mode == QE_ROUTER_QMAT && c->router_bits != 4 && c->router_bits != 8)
         QE_FAIL("router_bits=%d: only 4 and 8", c->router_bits);
     const int G = c->ep_size < 1 ? 1 : c->ep_size;
-    if (G > 64 || c->E % G) QE_FAIL("ep_size=%d must divide E=%d (at most 64)", c->ep_size, c->E);
+    if (G > 64) QE_FAIL("ep_size=%d above 64", c->ep_size);
     if (c->ep_rank < 0 || c->ep_rank >= G) QE_FAIL("ep_rank=%d outside [0, %d)", c->ep_rank, G);
-    if (c->E / G < 1) QE_FAIL("no experts per rank");
+    if (!c->placement) {
+        if (c->E % G) QE_FAIL("ep_size=%d must divide E=%d (or give a placement)", c->ep_size, c->E);
+        return 0;
+    }
+    if (G < 2) QE_FAIL("a placement needs ep_size > 1");
+    if (c->slots < 1 || c->slots > c->E) QE_FAIL("placement: slots=%d outside [1, E=%d]", c->slots, c->E);
+    std::vector<int> seen(c->E, 0), row(c->E, -1);
+    for (int r = 0; r < G; r++) {
+        int n = 0;
+        for (int j = 0; j < c->slots; j++) {
+            const int e = c->placement[(size_t)r * c->slots + j];
+            if (e == -1) continue;
+            if (e < 0 || e >= c->E) QE_FAIL("placement[%d][%d] = %d is not an expert id", r, j, e);
+            if (row[e] == r) QE_FAIL("placement: rank %d lists expert %d twice", r, e);
+            row[e] = r;
+            seen[e]++;
+            n++;
+        }
+        if (!n) QE_FAIL("placement: rank %d holds no expert", r);
+    }
+    for (int e = 0; e < c->E; e++)
+        if (!seen[e]) QE_FAIL("placement: expert %d is held by no rank", e);
     return 0;
+}
+
+/* The device placement table of a handle, [E][2 + G] int32: per expert its local slot on `rank` (-1 if not held
+ * there), its replica count and the ranks holding it, ascending (-1 past the count). */
+std::vector<int32_t> placement_table(const QeMoeConfig *c, int G, int rank, int32_t *held, int *n_held) {
+    const int E = c->E, W = 2 + G;
+    std::vector<int32_t> t((size_t)E * W, -1);
+    for (int e = 0; e < E; e++) t[(size_t)e * W + 1] = 0;
+    *n_held = 0;
+    for (int r = 0; r < G; r++) {
+        const int S = c->placement ? c->slots : E / G;
+        for (int j = 0; j < S; j++) {
+            const int e = c->placement ? c->placement[(size_t)r * S + j] : r * S + j;
+            if (e < 0) continue;
+            int32_t *te = &t[(size_t)e * W];
+            te[2 + te[1]++] = r;
+            if (r == rank) {
+                te[0] = *n_held;
+                held[(*n_held)++] = e;
+            }
+        }
+    }
+    return t;
 }
 
 size_t qbytes(int n, int rows, int cols, int bits, int gs, size_t *wb, size_t *gb) {
@@ -242,8 +325,10 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     if (m->cfg.max_tokens < 1) m->cfg.max_tokens = 4096;
     if (m->cfg.ep_size < 1) m->cfg.ep_size = 1;
     m->device = c->device;
-    m->E_loc = c->E / m->cfg.ep_size;
-    m->e0 = m->cfg.ep_rank * m->E_loc;
+    const int G = m->cfg.ep_size;
+    const std::vector<int32_t> table = placement_table(&m->cfg, G, m->cfg.ep_rank, m->held, &m->E_loc);
+    m->e0 = c->placement ? -1 : m->cfg.ep_rank * m->E_loc;
+    m->cfg.placement = nullptr;   /* the caller's table is not kept */
     const int E = c->E, El = m->E_loc, H = c->hidden, I = c->inter, Is = c->sh_inter, b = c->bits,
               gs = c->group_size;
     struct Part { int n, rows, cols, bits; QeQDev *dst; };
@@ -262,6 +347,8 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     const size_t wd_bytes = sizeof(float) * 2 * (size_t)H * qe_router_wd_rows(E);
     if (c->router_mode == QE_ROUTER_F32)
         total += align256(sizeof(float) * (size_t)(E + 1) * H) + align256(4 * (size_t)E) + align256(wd_bytes);
+    const size_t table_bytes = sizeof(int32_t) * table.size();
+    total += align256(table_bytes);
     char *base = nullptr;
     if (cudaMalloc((void **)&base, total) != cudaSuccess) {
         fprintf(stderr, "qengine_b200: cannot allocate %zu bytes of HBM for the block\n", total);
@@ -285,6 +372,13 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
         m->router_w = (float *)(base + off); off += align256(sizeof(float) * (size_t)(E + 1) * H);
         m->router_bias = (float *)(base + off); off += align256(4 * (size_t)E);
         m->router_wd = (float *)(base + off); off += align256(wd_bytes);
+    }
+    m->place = (int32_t *)(base + off); off += align256(table_bytes);
+    if (cudaMemcpy(m->place, table.data(), table_bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+        fprintf(stderr, "qengine_b200: cannot copy the placement table\n");
+        cudaFree(base);
+        free(m);
+        return nullptr;
     }
     m->ex.E = El; m->ex.k = c->top_k; m->ex.hidden = H; m->ex.inter = I; m->ex.sh_inter = Is;
     size_t wb, gb;
@@ -315,6 +409,30 @@ QeMoe *alloc_handle(const QeMoeConfig *c) {
     return m;
 }
 
+/* The routed-expert tensor q from local slot `slot` on (each expert's codes and its scales/biases are contiguous
+ * in both scale layouts). */
+QeQDev at_slot(const QeQDev &q, int slot) {
+    QeQDev r = q;
+    const size_t wpm = (size_t)q.rows * ((size_t)q.cols * q.bits / 32), gpm = (size_t)q.rows * (q.cols / q.group_size);
+    r.w += (size_t)slot * wpm;
+    r.scales += (size_t)slot * gpm;
+    r.biases += (size_t)slot * gpm;
+    return r;
+}
+
+/* f(slot, first, n) for each maximal run of local slots holding consecutive global ids first .. first + n - 1
+ * (one run for a contiguous range); stops at the first nonzero result. */
+template <class F>
+int for_runs(const QeMoe *m, F f) {
+    for (int j = 0; j < m->E_loc;) {
+        int n = 1;
+        while (j + n < m->E_loc && m->held[j + n] == m->held[j] + n) n++;
+        if (int rc = f(j, m->held[j], n)) return rc;
+        j += n;
+    }
+    return 0;
+}
+
 /* Copies matrices [first, first + n) of a host tensor into dst. */
 int upload_q(const QeQDev *dst, const QeQTensor *src0, int n, cudaStream_t s, int first = 0) {
     if (!src0->w || !src0->scales || !src0->biases) QE_FAIL("missing quantized tensor");
@@ -325,6 +443,9 @@ int upload_q(const QeQDev *dst, const QeQTensor *src0, int n, cudaStream_t s, in
     const QeQTensor *src = &src1;
     const size_t wb = (size_t)n * dst->rows * ((size_t)dst->cols * dst->bits / 32) * 4;
     const size_t gb = (size_t)n * dst->rows * (size_t)ng * 2;
+    page_in(src->w, wb);
+    page_in(src->scales, gb);
+    page_in(src->biases, gb);
     QE_CHECK(cudaMemcpyAsync((void *)dst->w, src->w, wb, cudaMemcpyHostToDevice, s));
     if (!dst->scale_t) {
         QE_CHECK(cudaMemcpyAsync((void *)dst->scales, src->scales, gb, cudaMemcpyHostToDevice, s));
@@ -432,10 +553,13 @@ QeMoe *qe_moe_create(const QeMoeConfig *cfg, const QeMoeWeights *w) {
     if (!m) return nullptr;
     DevCtx *d = &g_dev[m->device];
     cudaStream_t s = d->stream;
-    const int El = m->E_loc, e0 = m->e0;
-    int rc = upload_q(&m->ex.gate, &w->gate, El, s, e0) || upload_q(&m->ex.up, &w->up, El, s, e0) ||
-             upload_q(&m->ex.down, &w->down, El, s, e0) || upload_q(&m->ex.sh_gate, &w->sh_gate, 1, s) ||
-             upload_q(&m->ex.sh_up, &w->sh_up, 1, s) || upload_q(&m->ex.sh_down, &w->sh_down, 1, s);
+    int rc = for_runs(m, [&](int slot, int first, int n) {
+                 const QeQDev g = at_slot(m->ex.gate, slot), u = at_slot(m->ex.up, slot), dn = at_slot(m->ex.down, slot);
+                 return upload_q(&g, &w->gate, n, s, first) || upload_q(&u, &w->up, n, s, first) ||
+                        upload_q(&dn, &w->down, n, s, first);
+             }) ||
+             upload_q(&m->ex.sh_gate, &w->sh_gate, 1, s) || upload_q(&m->ex.sh_up, &w->sh_up, 1, s) ||
+             upload_q(&m->ex.sh_down, &w->sh_down, 1, s);
     if (!rc && cfg->router_mode == QE_ROUTER_QMAT)
         rc = upload_q(&m->router_q, &w->router_q, 1, s) || upload_q(&m->sh_router_q, &w->sh_router_q, 1, s);
     if (!rc && cfg->router_mode == QE_ROUTER_F32) {
@@ -472,8 +596,11 @@ QeMoe *qe_moe_create_synthetic(const QeMoeConfig *cfg, uint64_t seed, uint32_t b
         return qe_launch_synth_qmat(seed, block, stream, first, n, q.rows, q.cols, q.bits, gs, q.scale_t,
                                     (uint32_t *)q.w, (uint16_t *)q.scales, (uint16_t *)q.biases, s);
     };
-    const int El = m->E_loc, e0 = m->e0;
-    int rc = gen(m->ex.gate, SYN_GATE, El, e0) || gen(m->ex.up, SYN_UP, El, e0) || gen(m->ex.down, SYN_DOWN, El, e0) ||
+    int rc = for_runs(m, [&](int slot, int first, int n) {
+                 return gen(at_slot(m->ex.gate, slot), SYN_GATE, n, first) ||
+                        gen(at_slot(m->ex.up, slot), SYN_UP, n, first) ||
+                        gen(at_slot(m->ex.down, slot), SYN_DOWN, n, first);
+             }) ||
              gen(m->ex.sh_gate, SYN_SH_GATE, 1) || gen(m->ex.sh_up, SYN_SH_UP, 1) || gen(m->ex.sh_down, SYN_SH_DOWN, 1);
     (void)I; (void)Is; (void)b;
     if (!rc && cfg->router_mode == QE_ROUTER_QMAT)
@@ -649,21 +776,51 @@ __global__ void ep_meta_kernel(const int32_t *__restrict__ idx, const float *__r
     meta[(size_t)t * 2 * k + k + j] = __float_as_int(score[i]);
 }
 
-/* meta (global ids) -> local slot ids of the experts [e0, e0 + El) (-1 elsewhere) and the scores */
-__global__ void ep_local_kernel(const int32_t *__restrict__ meta, int n, int k, int e0, int El,
+/* The expert placement on the device: per expert e, place[e*W] = its local slot on this rank (-1: not held),
+ * place[e*W + 1] = replica count n, place[e*W + 2 ..] = the n holding ranks ascending (W = 2 + G). */
+struct EpPlace {
+    const int32_t *t;
+    int W;
+};
+
+EpPlace place_of(const QeMoe *m) { return {m->place, 2 + m->cfg.ep_size}; }
+
+/* The rank serving expert e for the token in row t of source rank src: replica (t + src) mod n. */
+__device__ __forceinline__ int ep_dest(EpPlace p, int e, int t, int src) {
+    const int32_t *te = p.t + (size_t)e * p.W;
+    const int n = te[1];
+    return te[2 + (n > 1 ? (t + src) % n : 0)];
+}
+
+/* meta -> local slot ids (-1 = not this rank's) and scores. Ids tagged QE_EP_ROUTED were routed here by the
+ * sender; untagged ids (the replicated step's own meta, row = token) count where replica (row, src 0) is
+ * this rank. */
+__global__ void ep_local_kernel(const int32_t *__restrict__ meta, int n, int k, int self, EpPlace pl,
                                 int32_t *__restrict__ idx, float *__restrict__ score) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n * k) return;
     const int t = i / k, j = i % k;
     const int e = meta[(size_t)t * 2 * k + j];
-    idx[i] = (e >= e0 && e < e0 + El) ? e - e0 : -1;
+    int s = -1;
+    if (e >= 0) {
+        const int g = e & ~QE_EP_ROUTED;
+        if (e & QE_EP_ROUTED) s = pl.t[(size_t)g * pl.W];
+        else if (ep_dest(pl, g, t, 0) == self) s = pl.t[(size_t)g * pl.W];
+    }
+    idx[i] = s;
     score[i] = __int_as_float(meta[(size_t)t * 2 * k + k + j]);
 }
 
+/* Slot j's id in the slot list sent to rank d: tagged if routed to d, else -1. */
+__device__ __forceinline__ int32_t ep_sent_id(EpPlace pl, int32_t e, int t, int src, int d) {
+    return e >= 0 && ep_dest(pl, e, t, src) == d ? (e | QE_EP_ROUTED) : -1;
+}
+
 /* One block per destination rank d: home[d][t] = the row of token t in block d (the tokens with at least one
- * expert on d, in token order) or -1, counts[d] = rows in block d. */
-__global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *__restrict__ meta, int T, int k, int El,
-                                                       int32_t *__restrict__ home, int32_t *__restrict__ counts) {
+ * slot routed to d, in token order) or -1, counts[d] = rows in block d. */
+__global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *__restrict__ meta, int T, int k, int src,
+                                                       EpPlace pl, int32_t *__restrict__ home,
+                                                       int32_t *__restrict__ counts) {
     const int d = blockIdx.x;
     __shared__ int wsum[32];
     __shared__ int base_s;
@@ -676,7 +833,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *__restrict
         if (t < T)
             for (int j = 0; j < k; j++) {
                 const int e = meta[(size_t)t * 2 * k + j];
-                f |= (e >= 0 && e / El == d) ? 1 : 0;
+                f |= (e >= 0 && ep_dest(pl, e, t, src) == d) ? 1 : 0;
             }
         int incl = f;
 #pragma unroll
@@ -706,11 +863,12 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t *__restrict
     if (tid == 0) counts[d] = base_s;
 }
 
-/* Warp (d, t): token t's row and meta to its row of block d; row t of block d, when at or past counts[d],
- * becomes padding (expert ids -1, scores 0). H % 4 == 0, 16-byte aligned rows. */
+/* Warp (d, t): token t's row and slot list (ids as ep_sent_id) to its row of block d; row t of block d, when at
+ * or past counts[d], becomes padding (expert ids -1, scores 0). H % 4 == 0, 16-byte aligned rows. */
 __global__ void ep_scatter_kernel(const float *__restrict__ x, const int32_t *__restrict__ meta, int T, int H, int k,
-                                  int G, const int32_t *__restrict__ home, const int32_t *__restrict__ counts,
-                                  float *__restrict__ send_x, int32_t *__restrict__ send_meta) {
+                                  int G, int self, EpPlace pl, const int32_t *__restrict__ home,
+                                  const int32_t *__restrict__ counts, float *__restrict__ send_x,
+                                  int32_t *__restrict__ send_meta) {
     const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (w >= (long long)G * T) return;
@@ -720,7 +878,10 @@ __global__ void ep_scatter_kernel(const float *__restrict__ x, const int32_t *__
         const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * H);
         float4 *dst = reinterpret_cast<float4 *>(send_x + ((size_t)d * T + pos) * H);
         for (int c = lane; c < H / 4; c += 32) dst[c] = src[c];
-        for (int c = lane; c < 2 * k; c += 32) send_meta[((size_t)d * T + pos) * 2 * k + c] = meta[(size_t)t * 2 * k + c];
+        for (int c = lane; c < 2 * k; c += 32) {
+            const int32_t v = meta[(size_t)t * 2 * k + c];
+            send_meta[((size_t)d * T + pos) * 2 * k + c] = c < k ? ep_sent_id(pl, v, t, self, d) : v;
+        }
     }
     if (t >= counts[d])
         for (int c = lane; c < 2 * k; c += 32) send_meta[((size_t)d * T + t) * 2 * k + c] = c < k ? -1 : 0;
@@ -828,7 +989,7 @@ int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sm
 /* Warp (d, t), peer-memory dispatch: token t's row and slot list go straight into rank d's receive buffers,
  * block `self`, row home[d][t]; row t of that block at or past counts[d] becomes padding. */
 __global__ void ep_scatter_p2p_kernel(const float *__restrict__ x, const int32_t *__restrict__ meta, int T, int H,
-                                      int k, int G, int self, const int32_t *__restrict__ home,
+                                      int k, int G, int self, EpPlace pl, const int32_t *__restrict__ home,
                                       const int32_t *__restrict__ counts, float *const *__restrict__ recv_x,
                                       int32_t *const *__restrict__ recv_meta) {
     const long long w = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -841,7 +1002,10 @@ __global__ void ep_scatter_p2p_kernel(const float *__restrict__ x, const int32_t
         float4 *dst = reinterpret_cast<float4 *>(recv_x[d] + ((size_t)self * T + pos) * H);
         for (int c = lane; c < H / 4; c += 32) dst[c] = src[c];
         int32_t *dm = recv_meta[d] + ((size_t)self * T + pos) * 2 * k;
-        for (int c = lane; c < 2 * k; c += 32) dm[c] = meta[(size_t)t * 2 * k + c];
+        for (int c = lane; c < 2 * k; c += 32) {
+            const int32_t v = meta[(size_t)t * 2 * k + c];
+            dm[c] = c < k ? ep_sent_id(pl, v, t, self, d) : v;
+        }
     }
     if (t >= counts[d]) {
         int32_t *dm = recv_meta[d] + ((size_t)self * T + t) * 2 * k;
@@ -874,8 +1038,8 @@ extern "C" {
 
 int qe_moe_forward_device(QeMoe *m, int T, const float *x, float *out, void *stream) {
     if (!m || !x || !out || T < 1) QE_FAIL("forward: bad arguments");
-    if (m->cfg.ep_size > 1) QE_FAIL("forward: this handle holds experts [%d, %d) only: use the qe_moe_ep_* calls",
-                                    m->e0, m->e0 + m->E_loc);
+    if (m->cfg.ep_size > 1) QE_FAIL("forward: this handle holds %d of the %d experts only: use the qe_moe_ep_* calls",
+                                    m->E_loc, m->cfg.E);
     DevCtx *d;
     if (dev_ctx(m->device, &d)) return -1;
     cudaStream_t s = (cudaStream_t)stream;
@@ -987,8 +1151,8 @@ void qe_moe_graph_free(QeMoeGraph *g) {
  * calls run under each other's kernels; every call computes what qe_moe_forward does. */
 int qe_moe_forward_async(QeMoe *m, int T, const float *x, float *out) {
     if (!m || !x || !out || T < 1) QE_FAIL("forward_async: bad arguments");
-    if (m->cfg.ep_size > 1) QE_FAIL("forward_async: this handle holds experts [%d, %d) only: use the qe_moe_ep_* calls",
-                                    m->e0, m->e0 + m->E_loc);
+    if (m->cfg.ep_size > 1) QE_FAIL("forward_async: this handle holds %d of the %d experts only: use the qe_moe_ep_* calls",
+                                    m->E_loc, m->cfg.E);
     if (T > m->cfg.max_tokens) QE_FAIL("forward_async: T=%d above the handle's max_tokens %d", T, m->cfg.max_tokens);
     DevCtx *d;
     if (dev_ctx(m->device, &d)) return -1;
@@ -1064,8 +1228,8 @@ int qe_moe_forward_wait(QeMoe *m) {
 
 int qe_moe_forward(QeMoe *m, int T, const float *x, float *out) {
     if (!m || !x || !out || T < 1) QE_FAIL("forward: bad arguments");
-    if (m->cfg.ep_size > 1) QE_FAIL("forward: this handle holds experts [%d, %d) only: use the qe_moe_ep_* calls",
-                                    m->e0, m->e0 + m->E_loc);
+    if (m->cfg.ep_size > 1) QE_FAIL("forward: this handle holds %d of the %d experts only: use the qe_moe_ep_* calls",
+                                    m->E_loc, m->cfg.E);
     DevCtx *d;
     if (dev_ctx(m->device, &d)) return -1;
     cudaStream_t s = d->stream;
@@ -1128,6 +1292,12 @@ int qe_moe_route(QeMoe *m, int T, const float *x, int32_t *idx, float *score) {
 
 int qe_moe_ep_size(const QeMoe *m) { return m ? m->cfg.ep_size : -1; }
 
+int qe_moe_ep_experts(const QeMoe *m, int32_t *ids) {
+    if (!m) return -1;
+    if (ids) memcpy(ids, m->held, sizeof(int32_t) * m->E_loc);
+    return m->E_loc;
+}
+
 int qe_moe_ep_route_device(QeMoe *m, int T, const float *x, int32_t *meta, float *shared, void *stream) {
     if (!m || !x || !meta || !shared || T < 1) QE_FAIL("ep_route: bad arguments");
     DevCtx *d;
@@ -1158,11 +1328,11 @@ int qe_moe_ep_pack_device(QeMoe *m, int T, const float *x, const int32_t *meta, 
     DevCtx *d;
     if (dev_ctx(m->device, &d)) return -1;
     cudaStream_t s = (cudaStream_t)stream;
-    ep_plan_kernel<<<G, 1024, 0, s>>>(meta, T, k, m->E_loc, home, counts);
+    ep_plan_kernel<<<G, 1024, 0, s>>>(meta, T, k, m->cfg.ep_rank, place_of(m), home, counts);
     QE_CHECK(cudaGetLastError());
     const long long threads = (long long)G * T * 32;
-    ep_scatter_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, meta, T, H, k, G, home, counts, send_x,
-                                                                       send_meta);
+    ep_scatter_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, meta, T, H, k, G, m->cfg.ep_rank,
+                                                                       place_of(m), home, counts, send_x, send_meta);
     QE_CHECK(cudaGetLastError());
     g_launches += 2;
     return 0;
@@ -1180,8 +1350,8 @@ int qe_moe_ep_experts_device(QeMoe *m, int n, const float *x, const int32_t *met
     scratch_layout(m->cfg, P, (char *)d->ws, &sc);
     for (int r0 = 0; r0 < n; r0 += P) {
         const int cnt = std::min(P, n - r0);
-        ep_local_kernel<<<(cnt * k + 255) / 256, 256, 0, s>>>(meta + (size_t)r0 * 2 * k, cnt, k, m->e0, m->E_loc,
-                                                             sc.idx, sc.score);
+        ep_local_kernel<<<(cnt * k + 255) / 256, 256, 0, s>>>(meta + (size_t)r0 * 2 * k, cnt, k, m->cfg.ep_rank,
+                                                             place_of(m), sc.idx, sc.score);
         QE_CHECK(cudaGetLastError());
         if (run_experts(m, x + (size_t)r0 * H, partial + (size_t)r0 * H, cnt, sc, d->sms, true, false, s)) return -1;
         g_launches += 1;
@@ -1380,11 +1550,12 @@ int qe_moe_ep_dispatch_p2p(QeMoe *m, QeEpXchg *xc, int T, const float *x, const 
     DevCtx *d;
     if (dev_ctx(m->device, &d)) return -1;
     cudaStream_t s = (cudaStream_t)stream;
-    ep_plan_kernel<<<G, 1024, 0, s>>>(meta, T, k, m->E_loc, home, counts);
+    ep_plan_kernel<<<G, 1024, 0, s>>>(meta, T, k, m->cfg.ep_rank, place_of(m), home, counts);
     QE_CHECK(cudaGetLastError());
     const long long threads = (long long)G * T * 32;
     ep_scatter_p2p_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
-        x, meta, T, H, k, G, m->cfg.ep_rank, home, counts, (float *const *)xc->dptr, (int32_t *const *)(xc->dptr + G));
+        x, meta, T, H, k, G, m->cfg.ep_rank, place_of(m), home, counts, (float *const *)xc->dptr,
+        (int32_t *const *)(xc->dptr + G));
     QE_CHECK(cudaGetLastError());
     xc->T = T;
     g_launches += 2;
@@ -1434,8 +1605,8 @@ int qe_moe_ep_experts_p2p(QeMoe *m, QeEpXchg *xc, int T, void *stream) {
         const int cnt = std::min(P, n - r0);
         const int cr = std::max(0, std::min(cnt, nr - r0));   /* received rows of this pass; the rest are own rows */
         if (cr > 0) {
-            ep_local_kernel<<<(cr * k + 255) / 256, 256, 0, s>>>(rm + (size_t)r0 * 2 * k, cr, k, m->e0, m->E_loc,
-                                                                sc.idx, sc.score);
+            ep_local_kernel<<<(cr * k + 255) / 256, 256, 0, s>>>(rm + (size_t)r0 * 2 * k, cr, k, m->cfg.ep_rank,
+                                                                place_of(m), sc.idx, sc.score);
             QE_CHECK(cudaGetLastError());
             g_launches += 1;
         }
@@ -1614,6 +1785,17 @@ int qe_ep_xchg_set_timeout_ms(QeEpXchg *x, int ms) {
 }
 
 double qe_expert_gb_read(void) { return (double)g_bytes_read.load() / 1e9; }
+
+int qe_set_threads(int n) {
+    if (n > 0) g_host_threads.store(n);
+    return host_threads();
+}
+
+double qe_peak_rss_gb(void) {
+    struct rusage ru;
+    if (getrusage(RUSAGE_SELF, &ru)) return -1.0;
+    return (double)ru.ru_maxrss * 1024.0 / 1073741824.0;   /* ru_maxrss: KiB on Linux */
+}
 double qe_expert_read_seconds(void) { return g_gpu_seconds; }
 int qe_device_count(void) {
     int n = 0;

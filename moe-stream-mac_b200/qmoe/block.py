@@ -31,13 +31,14 @@ class MoeBlock:
     def __init__(self, hidden: int, E: int, top_k: int, inter: int, sh_inter: int, bits: int, group_size: int = 64,
                  *, router_mode: int = QE_ROUTER_F32, router_bits: int = 8, max_tokens: int = 4096, device: int = 0,
                  layer: int = 0, weights: Mapping | None = None, seed: int | None = None, block: int = 0,
-                 router_bias: np.ndarray | None = None, ep_rank: int = 0, ep_size: int = 1):
+                 router_bias: np.ndarray | None = None, ep_rank: int = 0, ep_size: int = 1, placement=None):
         self.cfg = QeMoeConfig(hidden, E, top_k, inter, sh_inter, bits, group_size, router_mode, router_bits,
                                max_tokens, device, layer, ep_rank, ep_size)
         self.ep_rank, self.ep_size = ep_rank, ep_size
         self.hidden, self.top_k, self.E = hidden, top_k, E
         L = lib()
         self._keep = []
+        self._set_placement(placement)
         if weights is not None:
             w = QeMoeWeights()
             if router_mode == QE_ROUTER_F32:
@@ -67,7 +68,8 @@ class MoeBlock:
 
     @classmethod
     def from_safetensors(cls, directory: str, prefix: str, top_k: int, group_size: int = 64, *, max_tokens: int = 4096,
-                         device: int = 0, layer: int = 0, ep_rank: int = 0, ep_size: int = 1) -> "MoeBlock":
+                         device: int = 0, layer: int = 0, ep_rank: int = 0, ep_size: int = 1,
+                         placement=None) -> "MoeBlock":
         """One layer's block from an MLX checkpoint directory (qe_moe_open_safetensors): the shapes come
         from the tensors, e.g. prefix="language_model.model.layers.3.mlp"."""
         self = cls.__new__(cls)
@@ -75,6 +77,7 @@ class MoeBlock:
                                ep_rank, ep_size)
         self.ep_rank, self.ep_size = ep_rank, ep_size
         self._keep = []
+        self._set_placement(placement)
         self.handle = lib().qe_moe_open_safetensors(str(directory).encode(), prefix.encode(), C.byref(self.cfg))
         if not self.handle:
             raise EngineError("qe_moe_open_safetensors failed (see the message above)")
@@ -82,6 +85,23 @@ class MoeBlock:
         self.hidden, self.top_k = L.qe_moe_hidden(self.handle), top_k
         self.E = None
         return self
+
+    def _set_placement(self, placement) -> None:
+        """cfg.placement from a qmoe.placement.Placement or an int32 [ep_size][slots] table (None: contiguous)."""
+        if placement is None:
+            return
+        table = np.ascontiguousarray(getattr(placement, "table", placement), np.int32)
+        if table.ndim != 2:
+            raise ValueError("placement must be a [ep_size][slots] table")
+        self._keep.append(table)
+        self.cfg.placement, self.cfg.slots = table.ctypes.data, table.shape[1]
+
+    def held_experts(self) -> np.ndarray:
+        """Global ids of the routed experts this handle holds, in slot order (qe_moe_ep_experts)."""
+        n = lib().qe_moe_ep_experts(self.handle, None)
+        ids = np.empty(max(n, 0), np.int32)
+        lib().qe_moe_ep_experts(self.handle, iptr(ids))
+        return ids
 
     def close(self) -> None:
         if getattr(self, "handle", None):
@@ -156,6 +176,23 @@ class ForwardGraph:
     def launch(self, stream: int = 0) -> None:
         if lib().qe_moe_graph_launch(self.handle, C.c_void_p(stream)):
             raise EngineError("qe_moe_graph_launch failed")
+
+    def _set_placement(self, placement) -> None:
+        """cfg.placement from a qmoe.placement.Placement or an int32 [ep_size][slots] table (None: contiguous)."""
+        if placement is None:
+            return
+        table = np.ascontiguousarray(getattr(placement, "table", placement), np.int32)
+        if table.ndim != 2:
+            raise ValueError("placement must be a [ep_size][slots] table")
+        self._keep.append(table)
+        self.cfg.placement, self.cfg.slots = table.ctypes.data, table.shape[1]
+
+    def held_experts(self) -> np.ndarray:
+        """Global ids of the routed experts this handle holds, in slot order (qe_moe_ep_experts)."""
+        n = lib().qe_moe_ep_experts(self.handle, None)
+        ids = np.empty(max(n, 0), np.int32)
+        lib().qe_moe_ep_experts(self.handle, iptr(ids))
+        return ids
 
     def close(self) -> None:
         if getattr(self, "handle", None):

@@ -1,7 +1,8 @@
 """Expert parallelism: one routed MoE block sharded by expert over the ranks of a torch.distributed group.
 
 The reference runs the block in one process (engine/src/moe_layer.c:66-89). Here expert e lives on rank
-e // (E / world); the router and the shared expert are replicated. Two step shapes:
+e // (E / world), or where a placement table puts it (qmoe.placement: hot experts replicated on several
+ranks, each token served by one replica); the router and the shared expert are replicated. Step shapes:
 
 * token-sharded (prefill batches): every rank routes its own tokens, packs for each destination rank the rows
   of its tokens that have at least one expert there (token order, padded to T rows per destination so the
@@ -120,11 +121,32 @@ class ExpertParallelMoe:
 
     @classmethod
     def on_gpu(cls, cfg, rank: int, world: int, device: int, *, seed: int, block: int = 0, router_bias=None,
-               max_tokens: int = 4096, group=None) -> "ExpertParallelMoe":
-        """A synthetic block (qmoe.synth.MoeConfig shape) holding experts [rank*E/world, (rank+1)*E/world)."""
+               max_tokens: int = 4096, group=None, placement=None) -> "ExpertParallelMoe":
+        """A synthetic block (qmoe.synth.MoeConfig shape) holding experts [rank*E/world, (rank+1)*E/world), or
+        row `rank` of a qmoe.placement.Placement."""
         blk = MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, max_tokens=max_tokens,
-                       device=device, seed=seed, block=block, router_bias=router_bias, ep_rank=rank, ep_size=world)
+                       device=device, seed=seed, block=block, router_bias=router_bias, ep_rank=rank, ep_size=world,
+                       placement=placement)
         return cls(DeviceEngine(blk), rank, world, group, torch.device("cuda", device))
+
+    @staticmethod
+    def plan_placement(cfg, rank: int, world: int, device: int, x: torch.Tensor, spare_slots: int, *, seed: int,
+                       block: int = 0, router_bias=None, group=None):
+        """Plan a placement with `spare_slots` replica slots per rank from the routing of every rank's calibration
+        tokens x (collective): a contiguous handle routes x, the per-expert counts are summed over the ranks,
+        and qmoe.placement.Placement.from_load places E/world + spare_slots experts per rank."""
+        from .placement import Placement, histogram
+        if cfg.E % world:
+            raise ValueError("the calibration handle needs world to divide E")
+        blk = MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, max_tokens=x.shape[0],
+                       device=device, seed=seed, block=block, router_bias=router_bias, ep_rank=rank, ep_size=world)
+        try:
+            idx, _ = blk.route(x.cpu().numpy())
+        finally:
+            blk.close()
+        h = torch.from_numpy(histogram(idx, cfg.E)).to(torch.device("cuda", device))
+        dist.all_reduce(h, group=group)
+        return Placement.from_load(h.cpu().numpy(), world, min(cfg.E, cfg.E // world + spare_slots))
 
     def _empty(self, *shape, dtype=torch.float32):
         return torch.empty(*shape, dtype=dtype, device=self.device)

@@ -12,13 +12,14 @@ LIB_PATH = PKG / "lib" / "libqengine_b200.so"
 
 QE_ROUTER_F32 = 0
 QE_ROUTER_QMAT = 1
+QE_EP_ROUTED = 0x40000000   # tag of the slot ids routed to the destination rank in packed slot lists
 
 
 class QeMoeConfig(C.Structure):
     _fields_ = [("hidden", C.c_int), ("E", C.c_int), ("top_k", C.c_int), ("inter", C.c_int), ("sh_inter", C.c_int),
                 ("bits", C.c_int), ("group_size", C.c_int), ("router_mode", C.c_int), ("router_bits", C.c_int),
                 ("max_tokens", C.c_int), ("device", C.c_int), ("layer", C.c_int), ("ep_rank", C.c_int),
-                ("ep_size", C.c_int)]
+                ("ep_size", C.c_int), ("placement", C.c_void_p), ("slots", C.c_int)]
 
 
 class QeQTensor(C.Structure):
@@ -64,8 +65,10 @@ def lib() -> C.CDLL:
         L.qe_op_silu_mul.argtypes = [fp, fp, fp, C.c_int]
         L.qe_op_sigmoid.argtypes = [fp, fp, C.c_int]
         L.qe_op_expf.argtypes = [fp, fp, C.c_int]
-        for name in ("qe_expert_gb_read", "qe_expert_read_seconds"):
+        for name in ("qe_expert_gb_read", "qe_expert_read_seconds", "qe_peak_rss_gb"):
             getattr(L, name).restype = C.c_double
+        L.qe_set_threads.argtypes = [C.c_int]
+        L.qe_set_threads.restype = C.c_int
         L.qe_profile_begin.argtypes = [C.c_int]
         L.qe_profile_end.argtypes = [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_int)]
         L.qe_kernel_launches.restype = C.c_ulonglong
@@ -82,6 +85,7 @@ def lib() -> C.CDLL:
         L.qe_moe_ep_experts_device.argtypes = [vp, C.c_int, vp, vp, vp, vp]
         L.qe_moe_ep_combine_device.argtypes = [vp, C.c_int, vp, vp, vp, vp, vp]
         L.qe_moe_ep_size.argtypes = [vp]
+        L.qe_moe_ep_experts.argtypes = [vp, ip]
         L.qe_ep_xchg_create.restype = vp
         L.qe_ep_xchg_create.argtypes = [vp, C.c_int, vp]
         L.qe_ep_xchg_handle_bytes.restype = C.c_int

@@ -12,6 +12,9 @@ import numpy as np
 import torch
 
 import oracle
+from qmoe.placement import Placement
+
+ROUTED = 0x40000000   # QE_EP_ROUTED of include/qe_moe.h
 
 
 def _sigmoid(g: np.float32) -> np.float32:
@@ -22,12 +25,12 @@ def _sigmoid(g: np.float32) -> np.float32:
 
 
 class OracleEngine:
-    def __init__(self, blk: oracle.SynthBlock, rank: int, world: int):
+    def __init__(self, blk: oracle.SynthBlock, rank: int, world: int, placement: Placement | None = None):
         self.blk = blk
         self.hidden, self.top_k, self.E = blk.cfg.hidden, blk.cfg.top_k, blk.cfg.E
-        self.El = self.E // world
-        self.e0 = rank * self.El
-        self.world = world
+        self.place = placement or Placement.contiguous(self.E, world)
+        self.held = set(int(e) for e in self.place.table[rank] if e >= 0)
+        self.rank, self.world = rank, world
 
     def route(self, x: torch.Tensor, meta: torch.Tensor, shared: torch.Tensor) -> None:
         xn, k = x.numpy(), self.top_k
@@ -45,14 +48,16 @@ class OracleEngine:
         T, k, G = x.shape[0], self.top_k, self.world
         xn, m = x.numpy(), meta.numpy()
         sx, sm, hm, cn = send_x.numpy(), send_meta.numpy(), home.numpy(), counts.numpy()
+        dest = self.place.dest(m[:, :k], self.rank)   # the replica serving each slot (include/qe_moe.h rule)
         for d in range(G):
             n = 0
             for t in range(T):
                 ids = m[t, :k]
-                if np.any((ids >= 0) & (ids // self.El == d)):
+                if np.any(dest[t] == d):
                     hm[d, t] = n
                     sx[d, n] = xn[t]
-                    sm[d, n] = m[t]
+                    sm[d, n, :k] = np.where(dest[t] == d, ids | ROUTED, -1)
+                    sm[d, n, k:] = m[t, k:]
                     n += 1
                 else:
                     hm[d, t] = -1
@@ -66,7 +71,14 @@ class OracleEngine:
             o = np.zeros(self.hidden, np.float32)
             for j in range(k):
                 e = int(m[r, j])
-                if self.e0 <= e < self.e0 + self.El:
+                if e < 0:
+                    continue
+                if e & ROUTED:       # routed here by the sender
+                    mine = (e & ~ROUTED) in self.held
+                    e &= ~ROUTED
+                else:                # the replicated step's own rows: row r is token r, source rank 0
+                    mine = int(self.place.reps[e, r % self.place.nrep[e]]) == self.rank
+                if mine:
                     s = m[r, k + j:k + j + 1].view(np.float32)[0]
                     o = o + s * self.blk.expert(e, xn[r])
             p[r] = o

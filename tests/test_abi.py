@@ -72,3 +72,22 @@ def test_zipf_bias_is_a_seeded_permutation_of_a_zipf_law():
     assert b.max() == 0.0 and np.isclose(b.min(), -0.75 * 1.1 * np.log(256), rtol=1e-6)
     assert np.array_equal(b, zipf_router_bias(256, 1.1, seed=3))
     assert not np.array_equal(b, zipf_router_bias(256, 1.1, seed=4))
+
+
+def test_engine_thread_and_rss_calls_bind_as_qchat_does():
+    """qe_set_threads / qe_peak_rss_gb / the read statistics, bound with the argtypes and restypes of the
+    reference's terminal chat (engine/cli/qchat.py:46-48) on a fresh CDLL handle; no GPU needed."""
+    L = C.CDLL(str(qmoe.LIB_PATH))
+    L.qe_set_threads.argtypes = [C.c_int]
+    for name in ("qe_expert_gb_read", "qe_expert_read_seconds", "qe_peak_rss_gb"):
+        getattr(L, name).restype = C.c_double
+    default = L.qe_set_threads(0)          # n <= 0: keep, report the effective count
+    assert default >= 1
+    assert L.qe_set_threads(3) == 3
+    assert L.qe_set_threads(-1) == 3
+    assert L.qe_set_threads(default) == default
+    import resource
+    rss = L.qe_peak_rss_gb()
+    want = resource.getrusage(resource.RUSAGE_SELF).ru_maxrss / 2**20   # KiB -> GiB (Linux)
+    assert 0 < rss and abs(rss - want) <= 0.05 * want + 1e-3
+    assert L.qe_expert_gb_read() >= 0 and L.qe_expert_read_seconds() >= 0

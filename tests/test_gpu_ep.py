@@ -20,9 +20,9 @@ pytestmark = pytest.mark.gpu
 CFG = qmoe.MoeConfig("ep_small", hidden=512, inter=256, sh_inter=256, bits=4, tokens=64, E=32, top_k=4)
 
 
-def _blocks(cfg, G, seed=5):
+def _blocks(cfg, G, seed=5, router_bias=None, placement=None):
     return [qmoe.MoeBlock(cfg.hidden, cfg.E, cfg.top_k, cfg.inter, cfg.sh_inter, cfg.bits, seed=seed,
-                          ep_rank=r, ep_size=G) for r in range(G)]
+                          router_bias=router_bias, ep_rank=r, ep_size=G, placement=placement) for r in range(G)]
 
 
 def _emulated_sharded_step(blocks, xs):
@@ -162,6 +162,55 @@ def test_ep_vs_oracle():
         b.close()
 
 
+@pytest.mark.parametrize("G,T,extra", [(2, 40, 4), (4, 24, 2), (8, 16, 1), (8, 3, 2)])
+def test_ep_placement_emulated(G, T, extra):
+    """A placement planned from a Zipf-skewed calibration batch (qmoe.placement), `extra` spare slots per rank
+    holding replicas of the hot experts: each handle holds its row of the table, the rows sent to each rank are
+    those the host rule (replica (t + src) mod n) predicts, the sharded and peer-memory steps agree bit for bit,
+    and both steps and the replicated step match the single-handle forward."""
+    from qmoe.placement import Placement, histogram
+    bias = qmoe.zipf_router_bias(CFG.E, 1.1, seed=7)
+    ref = qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, router_bias=bias)
+    gen = torch.Generator().manual_seed(900 + G + T)
+    calib = torch.randn(256, CFG.hidden, generator=gen).numpy()
+    pl = Placement.from_load(histogram(ref.route(calib)[0], CFG.E), G, CFG.E // G + extra)
+    assert pl.nrep.max() > 1
+    blocks = _blocks(CFG, G, router_bias=bias, placement=pl)
+    for r, b in enumerate(blocks):
+        assert b.held_experts().tolist() == [int(e) for e in pl.table[r] if e >= 0]
+    xs = [torch.randn(T, CFG.hidden, generator=gen).cuda() for _ in range(G)]
+    outs, metas, counts = _emulated_sharded_step(blocks, xs)
+    # folded shared expert only where its batch takes the same kernels as the separate pass (T >= 5 rows: at
+    # T <= 4 the separate pass runs the decode GEMVs, the folded one the tensor-core kernels)
+    p2p = _emulated_p2p_step(blocks, xs, fold=T > 4)
+    k = CFG.top_k
+    for r in range(G):
+        want = ref.forward(xs[r].cpu().numpy())
+        idx = metas[r][:, :k]
+        dest = pl.dest(idx, r)
+        for d in range(G):
+            assert counts[r][d] == int(np.any(dest == d, axis=1).sum())
+        got = outs[r].cpu().numpy()
+        assert _rel(got, want).max() <= 5e-6
+        assert np.array_equal(p2p[r].view(np.uint32), got.view(np.uint32)), f"rank {r}"
+    # replicated step: the same tokens on every rank, the partials summed in rank order
+    from qmoe.ep import DeviceEngine
+    x = xs[0]
+    eng = [DeviceEngine(b) for b in blocks]
+    parts = torch.empty(G, T, CFG.hidden, device="cuda")
+    shared = torch.empty(T, CFG.hidden, device="cuda")
+    for r in range(G):
+        meta = torch.empty(T, 2 * k, dtype=torch.int32, device="cuda")
+        eng[r].route(x, meta, shared)
+        eng[r].experts(x, meta, parts[r])
+    out = torch.empty(T, CFG.hidden, device="cuda")
+    eng[0].combine(parts, None, shared, out)
+    torch.cuda.synchronize()
+    assert _rel(out.cpu().numpy(), ref.forward(x.cpu().numpy())).max() <= 5e-6
+    for b in blocks + [ref]:
+        b.close()
+
+
 def test_ep_refusals():
     b = qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, ep_rank=1, ep_size=2)
     x = np.zeros((2, CFG.hidden), np.float32)
@@ -172,6 +221,16 @@ def test_ep_refusals():
         qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, ep_rank=0, ep_size=3)
     with pytest.raises(qmoe.EngineError):
         qmoe.MoeBlock(CFG.hidden, CFG.E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, ep_rank=2, ep_size=2)
+    E = CFG.E
+    full = np.arange(E, dtype=np.int32).reshape(2, E // 2)
+    for bad in (full[:, :-1],                                   # an expert held by no rank
+                np.concatenate([full, full[:, :1]], axis=1),    # rank 0 lists expert 0 twice
+                np.where(full == 3, E, full)):                  # an id outside [0, E)
+        with pytest.raises(qmoe.EngineError):
+            qmoe.MoeBlock(CFG.hidden, E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, ep_rank=0, ep_size=2,
+                          placement=bad)
+    with pytest.raises(qmoe.EngineError):   # a placement needs ep_size > 1
+        qmoe.MoeBlock(CFG.hidden, E, CFG.top_k, CFG.inter, CFG.sh_inter, CFG.bits, seed=5, placement=full[:1])
 
 
 def _nccl_worker(rank, world, port, mode, q):

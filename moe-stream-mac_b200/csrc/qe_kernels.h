@@ -101,6 +101,8 @@ int qe_launch_synth_normal(uint64_t seed, uint32_t block, uint32_t stream, size_
                            cudaStream_t s);
 
 int qe_num_sms(void);
+/* Host threads for the library's CPU-side work (qe_set_threads; default: the hardware threads). */
+int qe_host_thread_count(void);
 
 /* Tensor-core (tcgen05) prefill path, expert_tc.cu. */
 #include <cuda_fp16.h>

@@ -1791,6 +1791,12 @@ int qe_set_threads(int n) {
     return host_threads();
 }
 
+}  // extern "C"
+
+int qe_host_thread_count(void) { return host_threads(); }
+
+extern "C" {
+
 double qe_peak_rss_gb(void) {
     struct rusage ru;
     if (getrusage(RUSAGE_SELF, &ru)) return -1.0;

@@ -12,10 +12,11 @@ from .lib import (QeMoeConfig, QeMoeWeights, QeQTensor, QE_ROUTER_F32, QE_ROUTER
 from .block import MoeBlock, EngineError
 from .synth import CONFIGS, MoeConfig, zipf_router_bias
 from .placement import Placement, histogram, histogram_from_trace, read_trace
+from .engine import Engine, ContextFull
 
 __all__ = ["QeMoeConfig", "QeMoeWeights", "QeQTensor", "QE_ROUTER_F32", "QE_ROUTER_QMAT", "LIB_PATH", "build", "lib",
            "qmat_matvec", "route_logits", "op_silu_mul", "op_sigmoid", "op_expf", "expert_gb_read",
            "expert_read_seconds", "device_count", "profile_begin", "profile_end",
            "kernel_launches", "graph_captures", "STAGES", "MoeBlock", "EngineError", "CONFIGS", "MoeConfig",
            "zipf_router_bias", "safetensors_tensor_info", "QE_EP_ROUTED", "Placement", "histogram",
-           "histogram_from_trace", "read_trace"]
+           "histogram_from_trace", "read_trace", "Engine", "ContextFull"]

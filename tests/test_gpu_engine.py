@@ -29,10 +29,12 @@ TOKENS = [5, 17, 200, 3, 3, 99, 250, 1, 64, 17]
 CHILD = r"""
 import ctypes as C, json, sys
 import numpy as np
-sys.path.insert(0, sys.argv[1])
-from test_engine_cpu import _qchat_bind
 a = json.loads(sys.argv[2])
-lib = _qchat_bind(a["lib"])
+lib = C.CDLL(a["lib"])          # bound as engine/cli/qchat.py:39-48 binds it
+lib.qe_load.restype = C.c_void_p
+lib.qe_load.argtypes = [C.c_char_p, C.c_int]
+lib.qe_forward.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_float)]
+lib.qe_vocab.argtypes = [C.c_void_p]
 h = lib.qe_load(a["dir"].encode(), a["max_len"])
 assert h, "reference qe_load failed"
 V = lib.qe_vocab(h)

@@ -21,6 +21,8 @@
  * the order differs from the reference's (tolerance 1e-5 rel-L2).
  */
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 #include "qe_common.cuh"
 #include "qe_kernels.h"
@@ -297,6 +299,206 @@ __global__ void __launch_bounds__(17 * 32) decode_down_combine_kernel(QeExpertAr
     du.end(a, h3, ldh, k, score, logits, ld_logits, out, smem, ys);
 }
 
+/* ------------------------------------------------------------------ coalesced decode GEMVs
+ * The expert stage of a decode step (a few tokens, one (token, slot) pair per unit) with every warp load
+ * coalesced: LPR lanes stream a row, each 16 bytes (CPL = 128 / BITS codes, inside one group of 64), so a warp
+ * load covers 32 * 16 contiguous bytes: RPW = 32 / LPR rows when a row is shorter than 512 bytes, or one
+ * 512-byte slice of a longer row (NS slices per row, one warp each). A lane's inputs are the same for every row
+ * it visits, so its CPL activations and their sum stay in registers; the unit's J row loads are all issued
+ * before the first is used. Per load, v = s * 2^b * (sum_i (1 + q_i/2^b) x_i - sum_i x_i) + bias * sum_i x_i
+ * over the lane's codes (qmat.c:43 per part of a group: the scale and bias of the group, the dot of its part),
+ * then the parts are summed across the row's lanes by a fixed transposed tree and across slices in order. */
+constexpr int kDgMaxSlices = 8;
+constexpr int kDgGuMaxWarps = 12;   /* gate/up CTA: 2 matrices x slices */
+constexpr int kDgDnMaxWarps = 18;   /* down CTA: (k + 1) slots x slices */
+
+/* Lane geometry of a row of K codes: lanes per row (1..32) and slices (rows of at least 512 bytes). */
+__host__ __device__ __forceinline__ int dg_lpr(int K, int bits) {
+    const int lanes = K * bits / 8 / 16;
+    return lanes < 32 ? lanes : 32;
+}
+__host__ __device__ __forceinline__ int dg_slices(int K, int bits) { return K * bits / 8 / 512; }
+/* Supported: every row a power-of-two number (2..16) of 16-byte lanes, or a whole number of 512-byte slices. */
+__host__ inline bool dg_supported(int K, int bits) {
+    if (K % kGS) return false;
+    const int lanes = K * bits / 8 / 16;
+    if (lanes >= 32) return lanes % 32 == 0 && lanes / 32 <= kDgMaxSlices;
+    return lanes >= 2 && (lanes & (lanes - 1)) == 0;
+}
+
+/* Transposed sum over the LPR lanes of a row of each of J values per lane: the levels pair lanes across lane
+ * bit LPR/2, then LPR/4, ... 1; while values remain, each level halves them (a lane keeps the lower or upper half
+ * by its bit), after that it adds the partner's single value. Lane l ends with value dg_index<LPR, J>(l). */
+template <int LPR, int J>
+__device__ __forceinline__ int dg_index(int lane) {
+    int idx = 0;
+#pragma unroll
+    for (int o = LPR / 2, w = J / 2; o; o >>= 1, w >>= 1)
+        if (w >= 1 && (lane & o)) idx += w;
+    return idx;
+}
+/* whether lane l holds the one copy of its value that is written (its full-exchange bits are clear) */
+template <int LPR, int J>
+__device__ __forceinline__ bool dg_writer(int lane) {
+    int mask = 0;
+#pragma unroll
+    for (int o = LPR / 2, w = J / 2; o; o >>= 1, w >>= 1)
+        if (w < 1) mask |= o;
+    return (lane & mask) == 0;
+}
+template <int LPR, int J>
+__device__ __forceinline__ float dg_reduce(float (&v)[J], int lane) {
+#pragma unroll
+    for (int o = LPR / 2, w = J / 2; o; o >>= 1, w >>= 1) {
+        if (w >= 1) {
+            const bool up = lane & o;
+#pragma unroll
+            for (int j = 0; j < w; j++) {
+                const float keep = up ? v[j + w] : v[j], give = up ? v[j] : v[j + w];
+                v[j] = __fadd_rn(keep, __shfl_xor_sync(QE_FULL, give, o));
+            }
+        } else {
+            v[0] = __fadd_rn(v[0], __shfl_xor_sync(QE_FULL, v[0], o));
+        }
+    }
+    return v[0];
+}
+
+/* One warp's unit: rows r0 + lane / LPR + RPW * j (j < J; rows past `rows` are clamped for the loads and not
+ * written) of matrix m for expert e, slice sl, against xv (the K activations in global memory). Returns this
+ * lane's reduced value; *row_out is its row, or -1 when the lane does not write. */
+template <int BITS, int LPR, int J>
+__device__ __forceinline__ float dg_unit(const QeQDev &m, int e, int r0, int sl, const float *__restrict__ xv,
+                                         int *row_out) {
+    constexpr int CPL = 128 / BITS, RPW = 32 / LPR;
+    const int lane = threadIdx.x & 31, rows = m.rows;
+    const int kl = (lane % LPR) * CPL + sl * 32 * CPL;          /* first input of this lane */
+    const int g = kl / kGS;
+    const size_t bpr = (size_t)m.cols * BITS / 8;
+    const uint8_t *base = reinterpret_cast<const uint8_t *>(m.w) + (size_t)e * rows * bpr + (size_t)kl * BITS / 8;
+    const int ng = m.cols / kGS;
+    const size_t so = m.scale_t ? ((size_t)e * ng + g) * rows : (size_t)e * rows * ng + g;
+    const size_t sstr = m.scale_t ? 1 : (size_t)ng;             /* between consecutive rows */
+    /* codes, scales and biases of the J rows: every load issued before the first use */
+    uint4 w[J];
+    uint32_t sb[J];
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        const int row = min(r0 + lane / LPR + RPW * j, rows - 1);
+        w[j] = __ldg(reinterpret_cast<const uint4 *>(base + (size_t)row * bpr));
+        sb[j] = (uint32_t)__ldg(m.scales + so + row * sstr) | ((uint32_t)__ldg(m.biases + so + row * sstr) << 16);
+    }
+    /* the lane's activations and their sum (a fixed left-to-right order) */
+    float xr[CPL];
+    const float4 *x4 = reinterpret_cast<const float4 *>(xv + kl);
+#pragma unroll
+    for (int i = 0; i < CPL / 4; i++) {
+        const float4 t = __ldg(x4 + i);
+        xr[4 * i] = t.x; xr[4 * i + 1] = t.y; xr[4 * i + 2] = t.z; xr[4 * i + 3] = t.w;
+    }
+    float xs = 0.0f;
+#pragma unroll
+    for (int i = 0; i < CPL; i++) xs = __fadd_rn(xs, xr[i]);
+    float v[J];
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        const uint32_t ws[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+        float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            if constexpr (BITS == 4) {
+                const float *xq = xr + 8 * q;
+                a0 = __ffma2_rn(make_float2(code_v<4, 0>(ws[q]), code_v<4, 1>(ws[q])), make_float2(xq[0], xq[1]), a0);
+                a1 = __ffma2_rn(make_float2(code_v<4, 2>(ws[q]), code_v<4, 3>(ws[q])), make_float2(xq[2], xq[3]), a1);
+                a0 = __ffma2_rn(make_float2(code_v<4, 4>(ws[q]), code_v<4, 5>(ws[q])), make_float2(xq[4], xq[5]), a0);
+                a1 = __ffma2_rn(make_float2(code_v<4, 6>(ws[q]), code_v<4, 7>(ws[q])), make_float2(xq[6], xq[7]), a1);
+            } else {
+                const float *xq = xr + 4 * q;
+                a0 = __ffma2_rn(make_float2(code_v<8, 0>(ws[q]), code_v<8, 1>(ws[q])), make_float2(xq[0], xq[1]), a0);
+                a1 = __ffma2_rn(make_float2(code_v<8, 2>(ws[q]), code_v<8, 3>(ws[q])), make_float2(xq[2], xq[3]), a1);
+            }
+        }
+        const float p = __fadd_rn(__fadd_rn(a0.x, a0.y), __fadd_rn(a1.x, a1.y));
+        const float sq = __fmul_rn(__fsub_rn(p, xs), (float)(1 << BITS));
+        const float s = __uint_as_float(sb[j] << 16), b = __uint_as_float(sb[j] & 0xFFFF0000u);
+        v[j] = __fmaf_rn(s, sq, __fmul_rn(b, xs));
+    }
+    const float r = dg_reduce<LPR, J>(v, lane);
+    const int row = r0 + lane / LPR + RPW * dg_index<LPR, J>(lane);
+    *row_out = (dg_writer<LPR, J>(lane) && row < rows) ? row : -1;
+    return r;
+}
+
+/* Rows per unit: J loads of RPW rows. */
+template <int LPR, int J>
+constexpr int dg_rows() { return J * (32 / LPR); }
+
+/* Gate/up + SwiGLU: CTA = (token-slot pair, block of dg_rows rows); warp (m, sl) = matrix m (gate, up), slice
+ * sl; the slices are summed in order, then h = silu(g) * u (ops.c:16-21) -> h3[p][row]. */
+template <int BITS, int LPR, int J>
+__global__ void __launch_bounds__(kDgGuMaxWarps * 32) dg_gateup_kernel(QeExpertArgs a, const float *__restrict__ x,
+                                                                        const int32_t *__restrict__ idx, int k,
+                                                                        float *__restrict__ h3, int ldh) {
+    constexpr int RU = dg_rows<LPR, J>();
+    __shared__ float part[2][kDgMaxSlices][RU];
+    const int p = blockIdx.x, t = p / (k + 1), j = p % (k + 1);
+    const bool shared = j == k;
+    const QeQDev &G = shared ? a.sh_gate : a.gate, &U = shared ? a.sh_up : a.up;
+    const int r0 = blockIdx.y * RU;
+    if (r0 >= G.rows) return;
+    const int e = shared ? 0 : idx[t * k + j];
+    const int ns = max(1, dg_slices(a.hidden, BITS)), warp = threadIdx.x >> 5;
+    const int m = warp / ns, sl = warp % ns;
+    int row;
+    const float v = dg_unit<BITS, LPR, J>(m ? U : G, e, r0, sl, x + (size_t)t * a.hidden, &row);
+    if (row >= 0) part[m][sl][row - r0] = v;
+    __syncthreads();
+    if (threadIdx.x < RU && r0 + threadIdx.x < G.rows) {
+        float gv = part[0][0][threadIdx.x], uv = part[1][0][threadIdx.x];
+        for (int i = 1; i < ns; i++) {
+            gv = __fadd_rn(gv, part[0][i][threadIdx.x]);
+            uv = __fadd_rn(uv, part[1][i][threadIdx.x]);
+        }
+        h3[(size_t)p * ldh + r0 + threadIdx.x] = qe_silu_mul(gv, uv);
+    }
+}
+
+/* Down + combine: CTA = (token, block of dg_rows output rows); warp (slot, sl) = slot (k routed experts, then the
+ * shared one), slice sl; slices summed in order, then out = sum_j score_j y_j (slot order) + sigmoid(shared-gate
+ * logit) y_shared (moe_layer.c:79-88). */
+template <int BITS, int LPR, int J>
+__global__ void __launch_bounds__(kDgDnMaxWarps * 32) dg_down_kernel(QeExpertArgs a, const float *__restrict__ h3, int ldh,
+                                                        const int32_t *__restrict__ idx,
+                                                        const float *__restrict__ score,
+                                                        const float *__restrict__ logits, int ld_logits, int k,
+                                                        float *__restrict__ out) {
+    constexpr int RU = dg_rows<LPR, J>();
+    extern __shared__ float ys[];                   /* [k + 1][ns][RU] */
+    const int t = blockIdx.x, H = a.hidden, r0 = blockIdx.y * RU, kp1 = k + 1;
+    const int ns = max(1, dg_slices(a.inter, BITS)), warp = threadIdx.x >> 5;
+    const int j = warp / ns, sl = warp % ns;
+    if (j < kp1) {
+        const bool shared = j == k;
+        int row;
+        const float v = dg_unit<BITS, LPR, J>(shared ? a.sh_down : a.down, shared ? 0 : idx[t * k + j], r0, sl,
+                                              h3 + ((size_t)t * kp1 + j) * ldh, &row);
+        if (row >= 0) ys[((size_t)j * ns + sl) * RU + row - r0] = v;
+    }
+    __syncthreads();
+    const int i = threadIdx.x;
+    if (i < RU && r0 + i < H) {
+        float o = 0.0f, ysh = 0.0f;
+        for (int jj = 0; jj < kp1; jj++) {
+            float y = ys[((size_t)jj * ns) * RU + i];
+            for (int s2 = 1; s2 < ns; s2++) y = __fadd_rn(y, ys[((size_t)jj * ns + s2) * RU + i]);
+            if (jj < k) o = __fadd_rn(o, __fmul_rn(score[t * k + jj], y));
+            else ysh = y;
+        }
+        o = __fadd_rn(o, __fmul_rn(qe_sigmoid(logits[(size_t)t * ld_logits + a.E]), ysh));
+        out[(size_t)t * H + r0 + i] = o;
+    }
+}
+
 /* ------------------------------------------------------------------ fused decode step */
 
 __device__ int g_decode_error;   /* first grid-barrier timeout code, read by qe_decode_error() */
@@ -417,8 +619,56 @@ bool qe_decode_supported(const QeExpertArgs *a) {
     return bh % kChunk == 0 && bh / kChunk >= kParts && bi % kChunk == 0 && a->inter % 4 == 0;
 }
 
+/* The coalesced GEMVs' launch, dispatched on the lanes per row (a template parameter). */
+template <int BITS, template <int, int, int> class Launch, int JMAX, typename... Args>
+static void dg_dispatch(int lpr, Args... args) {
+    switch (lpr) {
+    case 32: Launch<BITS, 32, JMAX>::run(args...); break;
+    case 16: Launch<BITS, 16, (JMAX < 16 ? JMAX : 16)>::run(args...); break;
+    case 8: Launch<BITS, 8, 8>::run(args...); break;
+    case 4: Launch<BITS, 4, 4>::run(args...); break;
+    default: Launch<BITS, 2, 2>::run(args...); break;
+    }
+}
+/* loads per lane and unit: 16 for gate/up (12 warps at most, 170 registers), 8 for the down projection
+ * (18 warps, 113 registers) */
+constexpr int kDgGuLoads = 16, kDgDnLoads = 8;
+template <int BITS, int LPR, int J>
+struct DgGateupLaunch {
+    static void run(const QeExpertArgs *a, const float *x, const int32_t *idx, int T, float *h3, int ldh, int ns,
+                    cudaStream_t s) {
+        constexpr int RU = dg_rows<LPR, J>();
+        const dim3 grid(T * (a->k + 1), (std::max(a->inter, a->sh_inter) + RU - 1) / RU);
+        dg_gateup_kernel<BITS, LPR, J><<<grid, 2 * ns * 32, 0, s>>>(*a, x, idx, a->k, h3, ldh);
+    }
+};
+template <int BITS, int LPR, int J>
+struct DgDownLaunch {
+    static void run(const QeExpertArgs *a, const float *h3, int ldh, const int32_t *idx, const float *score,
+                    const float *logits, int ld_logits, int T, float *out, int ns, cudaStream_t s) {
+        constexpr int RU = dg_rows<LPR, J>();
+        const int kp1 = a->k + 1;
+        const dim3 grid(T, (a->hidden + RU - 1) / RU);
+        dg_down_kernel<BITS, LPR, J><<<grid, kp1 * ns * 32, sizeof(float) * kp1 * ns * RU, s>>>(
+            *a, h3, ldh, idx, score, logits, ld_logits, a->k, out);
+    }
+};
+static bool dg_off() {
+    static const bool off = getenv("QE_DECODE_V1") && strcmp(getenv("QE_DECODE_V1"), "0") != 0;
+    return off;
+}
+
 int qe_launch_decode_gateup(const QeExpertArgs *a, const float *x, const int32_t *idx, int T, float *h3, int ldh,
                             cudaStream_t s) {
+    const int bits = a->gate.bits, K = a->hidden;
+    if (!dg_off() && (bits == 4 || bits == 8) && a->gate.group_size == kGS && dg_supported(K, bits) &&
+        2 * std::max(1, dg_slices(K, bits)) <= kDgGuMaxWarps) {
+        const int ns = std::max(1, dg_slices(K, bits));
+        if (bits == 4) dg_dispatch<4, DgGateupLaunch, kDgGuLoads>(dg_lpr(K, 4), a, x, idx, T, h3, ldh, ns, s);
+        else dg_dispatch<8, DgGateupLaunch, kDgGuLoads>(dg_lpr(K, 8), a, x, idx, T, h3, ldh, ns, s);
+        QE_CHECK(cudaGetLastError());
+        return 0;
+    }
     if (!qe_decode_supported(a)) QE_FAIL("decode gate/up: unsupported shape");
     dim3 grid(T * (a->k + 1), (a->inter + 31) / 32);
     const size_t smem = sizeof(float) * ((size_t)a->hidden + a->hidden / kGS);
@@ -433,6 +683,18 @@ int qe_launch_decode_gateup(const QeExpertArgs *a, const float *x, const int32_t
 int qe_launch_decode_down_combine(const QeExpertArgs *a, const float *h3, int ldh, const int32_t *idx,
                                   const float *score, const float *logits, int ld_logits, int T, float *out,
                                   cudaStream_t s) {
+    {
+        const int bits = a->down.bits, K = a->inter, ns = std::max(1, dg_slices(a->inter, a->down.bits));
+        if (!dg_off() && (bits == 4 || bits == 8) && a->down.group_size == kGS && a->sh_inter == K &&
+            dg_supported(K, bits) && (a->k + 1) * ns <= kDgDnMaxWarps) {
+            if (bits == 4)
+                dg_dispatch<4, DgDownLaunch, kDgDnLoads>(dg_lpr(K, 4), a, h3, ldh, idx, score, logits, ld_logits, T, out, ns, s);
+            else
+                dg_dispatch<8, DgDownLaunch, kDgDnLoads>(dg_lpr(K, 8), a, h3, ldh, idx, score, logits, ld_logits, T, out, ns, s);
+            QE_CHECK(cudaGetLastError());
+            return 0;
+        }
+    }
     if (!qe_decode_supported(a)) QE_FAIL("decode down: unsupported shape");
     const int K = a->inter, kp1 = a->k + 1;
     dim3 grid(T, (a->hidden + kDownRows - 1) / kDownRows);

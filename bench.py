@@ -287,7 +287,18 @@ def expert_kernel_name(cfg, stage: str, T: int) -> str:
               and bh % 128 == 0 and bh // 128 >= 8 and bi % 128 == 0)
     group = path == "group" and cfg.group_size == 64 and bh % 64 == 0 and bh // 64 >= 4 and bi % 64 == 0
     if decode:
-        return f"decode_gateup_kernel<{cfg.bits}>" if stage == "gateup" else f"decode_down_combine_kernel<{cfg.bits}>"
+        def coalesced(K: int, slots: int, max_warps: int) -> bool:
+            # the library's choice (decode.cu dg_supported): 16-byte lanes, a power of two (2..16) per row or
+            # whole 512-byte slices, and the CTA's warps within its bound
+            lanes = K * cfg.bits // 8 // 16
+            ok = (lanes >= 32 and lanes % 32 == 0 and lanes // 32 <= 8) or (2 <= lanes < 32 and lanes & (lanes - 1) == 0)
+            return (K % 64 == 0 and ok and slots * max(1, K * cfg.bits // 8 // 512) <= max_warps
+                    and os.environ.get("QE_DECODE_V1", "0") in ("", "0"))
+        if stage == "gateup":
+            return (f"dg_gateup_kernel<{cfg.bits}>" if coalesced(cfg.hidden, 2, 12)
+                    else f"decode_gateup_kernel<{cfg.bits}>")
+        return (f"dg_down_kernel<{cfg.bits}>" if coalesced(cfg.inter, cfg.top_k + 1, 18)
+                else f"decode_down_combine_kernel<{cfg.bits}>")
     if group:
         return f"group_gateup_kernel<{cfg.bits}>" if stage == "gateup" else f"group_down_kernel<{cfg.bits}>"
     if tc:

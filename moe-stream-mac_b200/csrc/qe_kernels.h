@@ -117,6 +117,7 @@ struct QeTcBufs {
 bool qe_tc_supported(const QeExpertArgs *a);
 size_t qe_tc_map_bytes(void);
 int qe_tc_weight_maps(const QeQDev *q, int n_experts, void *codes_map, void *sc_map, void *bi_map);
+int qe_launch_tc_prep(const QeExpertArgs *a, const float *x, int T, const QeTcBufs *tb, cudaStream_t s);
 int qe_launch_tc_gateup(const QeExpertArgs *a, const void *maps, const float *x, const QeBuckets *b, int T, int tn,
                         const QeTcBufs *t, int grid, cudaStream_t s);
 int qe_launch_tc_down(const QeExpertArgs *a, const void *maps, const QeBuckets *b, int T, int tn, const QeTcBufs *t,

@@ -6,9 +6,11 @@
  * One qwen3_5_moe MLX checkpoint, one token per qe_forward call (model.c:148-157): the embedding row, per
  * layer RMSNorm -> Gated DeltaNet or gated full attention -> residual -> RMSNorm -> routed MoE block ->
  * residual (model.c:135-146), the final RMSNorm and the LM head. The routed MoE blocks run on the GPU
- * (one qe_moe handle per layer, experts resident in HBM, include/qe_moe.h); the rest of the layer (the
- * "trunk") runs on the host in fp32 on qe_set_threads threads, with the checkpoint's trunk tensors
- * memory-mapped. Conventions as the reference's: NULL from qe_load with the reason on stderr; 0 ok, -1 error,
+ * (one qe_moe handle per layer, experts resident in HBM, include/qe_moe.h). The rest of the layer (the
+ * "trunk") runs on the same GPU by default: its tensors are copied to HBM at qe_load and a token's whole step
+ * stays on the device, the logits being the only copy back. With QE_TRUNK=host in the environment at qe_load,
+ * the trunk runs on the host in fp32 on qe_set_threads threads instead, reading the checkpoint's memory
+ * mappings. Conventions as the reference's: NULL from qe_load with the reason on stderr; 0 ok, -1 error,
  * -2 context full. qe_set_threads, qe_expert_gb_read, qe_expert_read_seconds and qe_peak_rss_gb (the rest of
  * qengine.h) are declared in qe_moe.h.
  */

@@ -32,6 +32,7 @@
 
 #include "ckpt.h"
 #include "qe_kernels.h"
+#include "trunk.h"
 #include "../../include/qe_engine.h"
 
 using namespace qe_ckpt;
@@ -471,7 +472,9 @@ struct QeModel {
     std::vector<float> x, h, t1, t2, gsum;
     std::vector<float> s1, s2, s3, s4, s5, s6;   /* per-layer scratch */
     int max_len = 0, pos = 0;
+    GpuTrunk *gt = nullptr;   /* the trunk on the GPU (default), or null: the host trunk (QE_TRUNK=host) */
     ~QeModel() {
+        if (gt) qe_gtrunk_free(gt);
         for (auto &L : layers)
             if (L.moe) qe_moe_free(L.moe);
     }
@@ -706,6 +709,38 @@ int load_model(QeModel *m, const char *dir, int max_len) {
     m->s4.assign(std::max<size_t>(big, KVD), 0.0f);
     m->s5.assign(std::max<size_t>((size_t)4 * c.lin_Hv, KVD), 0.0f);
     m->s6.assign(std::max<size_t>((size_t)c.Hq * max_len, (size_t)c.lin_Dv), 0.0f);
+    /* the trunk on the GPU, beside the MoE blocks, unless QE_TRUNK=host */
+    const char *tr = getenv("QE_TRUNK");
+    if (!tr || strcmp(tr, "host") != 0) {
+        auto hq = [](const HQ &q) {
+            TkHostQ t;
+            t.w = q.w; t.s = q.s; t.b = q.b; t.rows = q.rows; t.cols = q.cols; t.bits = q.bits; t.gs = q.gs;
+            return t;
+        };
+        TkDims d{};
+        d.hidden = c.hidden; d.vocab = c.vocab; d.Hq = c.Hq; d.Hkv = c.Hkv; d.D = c.head_dim; d.rot = c.rot_dims;
+        d.lin_Hk = c.lin_Hk; d.lin_Hv = c.lin_Hv; d.lin_Dk = c.lin_Dk; d.lin_Dv = c.lin_Dv; d.conv_K = c.conv_K;
+        d.max_len = max_len; d.eps = c.eps; d.theta = c.rope_theta;
+        std::vector<TkLayerHost> lh(m->layers.size());
+        for (size_t l = 0; l < m->layers.size(); l++) {
+            const Layer &L = m->layers[l];
+            TkLayerHost &h = lh[l];
+            h.linear = L.linear;
+            h.in_norm = L.in_norm.data();
+            h.post_norm = L.post_norm.data();
+            h.moe = L.moe;
+            if (L.linear) {
+                h.qkv = hq(L.g.qkv); h.z = hq(L.g.z); h.a = hq(L.g.a); h.b = hq(L.g.b); h.out = hq(L.g.out);
+                h.conv_w = L.g.conv_w.data(); h.A_log = L.g.A_log.data(); h.dt_bias = L.g.dt_bias.data();
+                h.norm_w = L.g.norm_w.data();
+            } else {
+                h.q = hq(L.a.q); h.k = hq(L.a.k); h.v = hq(L.a.v); h.o = hq(L.a.o);
+                h.q_norm = L.a.q_norm.data(); h.k_norm = L.a.k_norm.data();
+            }
+        }
+        m->gt = qe_gtrunk_create(d, hq(m->embed), hq(m->lm_head), m->final_norm.data(), lh, dev);
+        if (!m->gt) QE_FAIL("engine: the GPU trunk was not created (QE_TRUNK=host runs the trunk on the host)");
+    }
     return 0;
 }
 
@@ -727,6 +762,7 @@ void qe_free(QeModel *m) { delete m; }
 
 void qe_reset(QeModel *m) {
     if (!m) return;
+    if (m->gt && qe_gtrunk_reset(m->gt)) fprintf(stderr, "qengine_b200: qe_reset: GPU trunk reset failed\n");
     for (auto &L : m->layers) {
         if (L.linear) {
             std::fill(L.g.conv_state.begin(), L.g.conv_state.end(), 0.0f);
@@ -743,6 +779,12 @@ int qe_forward(QeModel *m, int token, float *logits) {
     if (m->pos >= m->max_len) return -2;
     const Cfg &c = m->c;
     const int H = c.hidden;
+    if (m->gt) {
+        if (token < 0 || token >= c.vocab) return -1;
+        if (qe_gtrunk_forward(m->gt, token, m->pos, logits)) return -1;
+        m->pos++;
+        return 0;
+    }
     if (hq_row(m->embed, token, m->x.data())) return -1;
     for (auto &L : m->layers) {
         rmsnorm(m->t1.data(), m->x.data(), L.in_norm.data(), H, c.eps);

@@ -1229,6 +1229,26 @@ int qe_moe_forward_wait(QeMoe *m) {
     return 0;
 }
 
+/* For a caller that runs qe_moe_forward_device inside its own step (the GPU trunk of the whole-model API): what
+ * qe_moe_forward does after a decode batch of T tokens -- the selected experts' bytes added to the read statistics
+ * (T * top_k experts, as qe_moe_forward counts a decode batch) and, when QE_TRACE is set, the step's routing
+ * appended to the trace file (read back after the stream's work so far; T within one pass of the handle). */
+int qe_moe_note_device_forward(QeMoe *m, int T, void *stream) {
+    if (!m || T < 1) return -1;
+    g_bytes_read += (unsigned long long)T * m->cfg.top_k * (unsigned long long)m->expert_bytes;
+    if (!getenv("QE_TRACE") || T > m->cfg.max_tokens) return 0;
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    Scratch sc;
+    scratch_layout(m->cfg, std::min(T, m->cfg.max_tokens), (char *)d->ws, &sc);
+    std::vector<int32_t> idx((size_t)T * m->cfg.top_k);
+    cudaStream_t s = (cudaStream_t)stream;
+    QE_CHECK(cudaMemcpyAsync(idx.data(), sc.idx, 4 * idx.size(), cudaMemcpyDeviceToHost, s));
+    QE_CHECK(cudaStreamSynchronize(s));
+    trace_route(m, idx.data(), T);
+    return 0;
+}
+
 int qe_moe_forward(QeMoe *m, int T, const float *x, float *out) {
     if (!m || !x || !out || T < 1) QE_FAIL("forward: bad arguments");
     if (m->cfg.ep_size > 1) QE_FAIL("forward: this handle holds %d of the %d experts only: use the qe_moe_ep_* calls",

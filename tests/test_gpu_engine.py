@@ -3,7 +3,8 @@
 A tiny synthetic qwen3_5_moe checkpoint (tests/model_synth.py: Gated DeltaNet and full-attention layers, routed
 MoE blocks with an 8-bit quantized router) is run token by token through the reference's unmodified qe_load /
 qe_forward (engine/src/qengine.c, compiled from its sources into oracle/_ref/libqengine_ref.so, in a child
-process) and through libqengine_b200's (host trunk, GPU MoE blocks), both bound with the reference front end's
+process) and through libqengine_b200's (trunk on the GPU by default, or on the host with QE_TRUNK=host; MoE
+blocks on the GPU), both bound with the reference front end's
 ctypes declarations (engine/cli/qchat.py:39-48). The logits must agree within fp32 reordering at every
 position, with the same arg-max token; the position, reset and context-full (-2) conventions must match.
 """
@@ -67,8 +68,10 @@ def _ours(lib, h, tokens, V):
     return out
 
 
+@pytest.mark.parametrize("trunk", ["gpu", "host"])
 @pytest.mark.parametrize("bits,interval", [(4, 4), (8, 2)])
-def test_engine_matches_reference_engine(tmp_path, bits, interval):
+def test_engine_matches_reference_engine(tmp_path, monkeypatch, bits, interval, trunk):
+    monkeypatch.setenv("QE_TRUNK", trunk)                     # read by qe_load
     m = TinyModel(bits=bits, full_attention_interval=interval)
     d = tmp_path / "model"
     write_tiny_model(d, m, seed=bits)

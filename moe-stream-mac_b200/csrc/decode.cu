@@ -499,6 +499,28 @@ __global__ void __launch_bounds__(kDgDnMaxWarps * 32) dg_down_kernel(QeExpertArg
     }
 }
 
+/* y = W x for one activation vector and a plain quantized matrix (the whole-model trunk's projections and LM
+ * head): CTA = a block of dg_rows rows, one warp per 512-byte slice of the rows; slices summed in order. */
+constexpr int kDgMvMaxWarps = 8;
+template <int BITS, int LPR, int J>
+__global__ void __launch_bounds__(kDgMvMaxWarps * 32) dg_matvec_kernel(QeQDev m, const float *__restrict__ x,
+                                                                      float *__restrict__ y) {
+    constexpr int RU = dg_rows<LPR, J>();
+    __shared__ float part[kDgMvMaxWarps][RU];
+    const int r0 = blockIdx.x * RU;
+    const int ns = max(1, dg_slices(m.cols, BITS)), sl = threadIdx.x >> 5;
+    int row;
+    const float v = dg_unit<BITS, LPR, J>(m, 0, r0, sl, x, &row);
+    if (row >= 0) part[sl][row - r0] = v;
+    __syncthreads();
+    const int i = threadIdx.x;
+    if (i < RU && r0 + i < m.rows) {
+        float acc = part[0][i];
+        for (int q = 1; q < ns; q++) acc = __fadd_rn(acc, part[q][i]);
+        y[r0 + i] = acc;
+    }
+}
+
 /* ------------------------------------------------------------------ fused decode step */
 
 __device__ int g_decode_error;   /* first grid-barrier timeout code, read by qe_decode_error() */
@@ -619,6 +641,14 @@ bool qe_decode_supported(const QeExpertArgs *a) {
     return bh % kChunk == 0 && bh / kChunk >= kParts && bi % kChunk == 0 && a->inter % 4 == 0;
 }
 
+template <int BITS, int LPR, int J>
+struct DgMatvecLaunch {
+    static void run(const QeQDev *m, const float *x, float *y, int ns, cudaStream_t s) {
+        constexpr int RU = dg_rows<LPR, J>();
+        dg_matvec_kernel<BITS, LPR, J><<<(m->rows + RU - 1) / RU, ns * 32, 0, s>>>(*m, x, y);
+    }
+};
+
 /* The coalesced GEMVs' launch, dispatched on the lanes per row (a template parameter). */
 template <int BITS, template <int, int, int> class Launch, int JMAX, typename... Args>
 static void dg_dispatch(int lpr, Args... args) {
@@ -656,6 +686,19 @@ struct DgDownLaunch {
 static bool dg_off() {
     static const bool off = getenv("QE_DECODE_V1") && strcmp(getenv("QE_DECODE_V1"), "0") != 0;
     return off;
+}
+
+/* y = W x (one vector) on the coalesced GEMV: 1 when the shape is not covered (the caller then uses
+ * qe_launch_qmatvec), 0 launched, -1 error. */
+int qe_launch_dg_matvec(const QeQDev *m, const float *x, float *y, cudaStream_t s) {
+    const int bits = m->bits, K = m->cols;
+    if (dg_off() || (bits != 4 && bits != 8) || m->group_size != kGS || !dg_supported(K, bits)) return 1;
+    const int ns = std::max(1, dg_slices(K, bits));
+    if (ns > kDgMvMaxWarps) return 1;
+    if (bits == 4) dg_dispatch<4, DgMatvecLaunch, kDgGuLoads>(dg_lpr(K, 4), m, x, y, ns, s);
+    else dg_dispatch<8, DgMatvecLaunch, kDgGuLoads>(dg_lpr(K, 8), m, x, y, ns, s);
+    QE_CHECK(cudaGetLastError());
+    return 0;
 }
 
 int qe_launch_decode_gateup(const QeExpertArgs *a, const float *x, const int32_t *idx, int T, float *h3, int ldh,

@@ -91,6 +91,8 @@ int qe_launch_decode_down_combine(const QeExpertArgs *a, const float *h3, int ld
 
 /* Generic quantized matrix-vector products (engine/src/qmat.c:15-49 semantics) over T vectors. */
 int qe_launch_qmatvec(const QeQDev *m, const float *x, int T, float *y, cudaStream_t s);
+/* y = W x on the coalesced decode GEMV (decode.cu): 1 when the shape is not covered, 0 launched, -1 error. */
+int qe_launch_dg_matvec(const QeQDev *m, const float *x, float *y, cudaStream_t s);
 
 /* Synthetic weights generated in HBM (csrc/synth.h). */
 int qe_launch_synth_qmat(uint64_t seed, uint32_t block, uint32_t stream, int first, int n, int rows, int cols,

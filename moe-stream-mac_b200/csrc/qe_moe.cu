@@ -1231,22 +1231,36 @@ int qe_moe_forward_wait(QeMoe *m) {
 
 /* For a caller that runs qe_moe_forward_device inside its own step (the GPU trunk of the whole-model API): what
  * qe_moe_forward does after a decode batch of T tokens -- the selected experts' bytes added to the read statistics
- * (T * top_k experts, as qe_moe_forward counts a decode batch) and, when QE_TRACE is set, the step's routing
- * appended to the trace file (read back after the stream's work so far; T within one pass of the handle). */
-int qe_moe_note_device_forward(QeMoe *m, int T, void *stream) {
+ * (T * top_k experts, as qe_moe_forward counts a decode batch) and, when QE_TRACE is set and a stream is given, the
+ * step's routing appended to the trace file (read back from the workspace the forward used -- ws, or the device's
+ * shared one when null -- after the stream's work so far; T within one pass). */
+int qe_moe_note_device_forward(QeMoe *m, int T, void *ws, void *stream) {
     if (!m || T < 1) return -1;
     g_bytes_read += (unsigned long long)T * m->cfg.top_k * (unsigned long long)m->expert_bytes;
-    if (!getenv("QE_TRACE") || T > m->cfg.max_tokens) return 0;
+    if (!stream || !getenv("QE_TRACE") || T > m->cfg.max_tokens) return 0;   /* no stream: statistics only */
     DevCtx *d;
     if (dev_ctx(m->device, &d)) return -1;
     Scratch sc;
-    scratch_layout(m->cfg, std::min(T, m->cfg.max_tokens), (char *)d->ws, &sc);
+    scratch_layout(m->cfg, std::min(T, m->cfg.max_tokens), ws ? (char *)ws : (char *)d->ws, &sc);
     std::vector<int32_t> idx((size_t)T * m->cfg.top_k);
     cudaStream_t s = (cudaStream_t)stream;
     QE_CHECK(cudaMemcpyAsync(idx.data(), sc.idx, 4 * idx.size(), cudaMemcpyDeviceToHost, s));
     QE_CHECK(cudaStreamSynchronize(s));
     trace_route(m, idx.data(), T);
     return 0;
+}
+
+/* qe_moe_forward_device on a workspace of the caller's (qe_moe_ws_bytes(m, T) bytes of device memory): for a
+ * caller that captures its own step in a CUDA graph, whose pointers must not move when the device's shared
+ * workspace grows for another call. */
+size_t qe_moe_ws_bytes(const QeMoe *m, int T) {
+    return m && T > 0 ? scratch_layout(m->cfg, std::min(T, m->cfg.max_tokens), nullptr, nullptr) : 0;
+}
+int qe_moe_forward_device_ws(QeMoe *m, int T, const float *x, float *out, void *ws, void *stream) {
+    if (!m || !x || !out || !ws || T < 1 || m->cfg.ep_size > 1) QE_FAIL("forward_ws: bad arguments");
+    DevCtx *d;
+    if (dev_ctx(m->device, &d)) return -1;
+    return forward_ws(m, T, x, out, (char *)ws, d->sms, (cudaStream_t)stream);
 }
 
 int qe_moe_forward(QeMoe *m, int T, const float *x, float *out) {

@@ -580,6 +580,56 @@ __global__ void router_qmat_exact_kernel(QeQDev m, int row_base, const float *__
     if (lane == 0) logits[(size_t)t * ld + row_base + row] = total;
 }
 
+/* The same arithmetic for a compile-time code width and group size: the group's code words loaded up front, the
+ * activations as float4, codes extracted with constant shifts; the two sums keep their sequential order. */
+template <int BITS, int GS>
+__global__ void router_qmat_exact_t_kernel(QeQDev m, int row_base, const float *__restrict__ x, int T, int H, int ld,
+                                           float *__restrict__ logits) {
+    constexpr int PER = 32 / BITS, WPG = GS * BITS / 32;
+    constexpr uint32_t kMask = (1u << BITS) - 1u;
+    const int lane = threadIdx.x & 31;
+    const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int row = (int)(wid % m.rows), t = (int)(wid / m.rows);
+    if (t >= T) return;
+    const int ng = m.cols / GS, wpr = m.cols * BITS / 32;
+    const uint32_t *wp = m.w + (size_t)row * wpr;
+    const float *xv = x + (size_t)t * H;
+    float total = 0.0f;
+    for (int g0 = 0; g0 < ng; g0 += 32) {
+        const int g = g0 + lane;
+        float tg = 0.0f;
+        if (g < ng) {
+            uint32_t w[WPG];
+            const uint4 *gw4 = reinterpret_cast<const uint4 *>(wp + (size_t)g * WPG);
+#pragma unroll
+            for (int i = 0; i < WPG / 4; i++) {
+                const uint4 u = __ldg(gw4 + i);
+                w[4 * i] = u.x; w[4 * i + 1] = u.y; w[4 * i + 2] = u.z; w[4 * i + 3] = u.w;
+            }
+            const float4 *x4 = reinterpret_cast<const float4 *>(xv + (size_t)g * GS);
+            float gsum = 0.0f, sq = 0.0f;
+#pragma unroll
+            for (int c = 0; c < GS / 4; c++) {
+                const float4 v = __ldg(x4 + c);
+                const float xs[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int j = 4 * c + u;
+                    gsum = __fadd_rn(gsum, xs[u]);
+                    const float q = (float)((w[j / PER] >> ((j % PER) * BITS)) & kMask);
+                    sq = __fadd_rn(sq, __fmul_rn(q, xs[u]));
+                }
+            }
+            const float s = qe_bf16_to_f32(m.scales[(size_t)row * ng + g]);
+            const float b = qe_bf16_to_f32(m.biases[(size_t)row * ng + g]);
+            tg = __fadd_rn(__fmul_rn(s, sq), __fmul_rn(b, gsum));
+        }
+        const int nsrc = min(32, ng - g0);
+        for (int src = 0; src < nsrc; src++) total = __fadd_rn(total, __shfl_sync(QE_FULL, tg, src));
+    }
+    if (lane == 0) logits[(size_t)t * ld + row_base + row] = total;
+}
+
 constexpr int kRouteWarps = 4;
 
 /* Softmax + top-k + renormalisation: one warp per token (route_topk_warp). */
@@ -693,15 +743,30 @@ int qe_launch_router_f32(const float *W, const float *bias, const float *x, int 
     return launches;
 }
 
+/* One quantized router matrix's logits: the templated kernel for the usual code widths and group sizes (16-byte
+ * aligned rows of codes and activations), the general one otherwise; the arithmetic is the same. */
+static int launch_router_qmat_one(const QeQDev *m, int row_base, const float *x, int T, int H, int ld, float *logits,
+                                  cudaStream_t s) {
+    const long long warps = (long long)m->rows * T;
+    const unsigned grid = (unsigned)((warps + 3) / 4);
+    const bool aligned = H % 4 == 0 && ((uintptr_t)x % 16) == 0 && ((uintptr_t)m->w % 16) == 0 &&
+                         (m->cols * m->bits / 32) % 4 == 0;
+    const int b = m->bits, gs = m->group_size;
+    if (aligned && b == 4 && gs == 64) router_qmat_exact_t_kernel<4, 64><<<grid, 128, 0, s>>>(*m, row_base, x, T, H, ld, logits);
+    else if (aligned && b == 8 && gs == 64) router_qmat_exact_t_kernel<8, 64><<<grid, 128, 0, s>>>(*m, row_base, x, T, H, ld, logits);
+    else if (aligned && b == 4 && gs == 32) router_qmat_exact_t_kernel<4, 32><<<grid, 128, 0, s>>>(*m, row_base, x, T, H, ld, logits);
+    else if (aligned && b == 8 && gs == 32) router_qmat_exact_t_kernel<8, 32><<<grid, 128, 0, s>>>(*m, row_base, x, T, H, ld, logits);
+    else if (aligned && b == 4 && gs == 128) router_qmat_exact_t_kernel<4, 128><<<grid, 128, 0, s>>>(*m, row_base, x, T, H, ld, logits);
+    else if (aligned && b == 8 && gs == 128) router_qmat_exact_t_kernel<8, 128><<<grid, 128, 0, s>>>(*m, row_base, x, T, H, ld, logits);
+    else router_qmat_exact_kernel<<<grid, 128, 0, s>>>(*m, row_base, x, T, H, ld, logits);
+    QE_CHECK(cudaGetLastError());
+    return 0;
+}
+
 int qe_launch_router_qmat(const QeQDev *router, const QeQDev *sh_router, const float *x, int T, int H, int E,
                           float *logits, cudaStream_t s) {
-    const long long warps = (long long)router->rows * T;
-    router_qmat_exact_kernel<<<(unsigned)((warps + 3) / 4), 128, 0, s>>>(*router, 0, x, T, H, E + 1, logits);
-    QE_CHECK(cudaGetLastError());
-    if (sh_router) {
-        router_qmat_exact_kernel<<<(T + 3) / 4, 128, 0, s>>>(*sh_router, E, x, T, H, E + 1, logits);
-        QE_CHECK(cudaGetLastError());
-    }
+    if (launch_router_qmat_one(router, 0, x, T, H, E + 1, logits, s)) return -1;
+    if (sh_router && launch_router_qmat_one(sh_router, E, x, T, H, E + 1, logits, s)) return -1;
     return 0;
 }
 

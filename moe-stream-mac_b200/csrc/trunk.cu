@@ -22,7 +22,7 @@
 
 namespace {
 
-constexpr int kNormThreads = 256;
+constexpr int kNormThreads = 1024;
 
 __device__ __forceinline__ float tk_silu(float v) { return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v))); }
 __device__ __forceinline__ float tk_sigmoid(float v) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))); }
@@ -63,9 +63,10 @@ __device__ __forceinline__ uint32_t tk_code(const uint32_t *row, int j, int bits
 }
 
 /* Embedding row `token` dequantized (qmat_row.c): x[c] = q * scale + bias, MLX layout [rows][groups]. */
-__global__ void tk_embed_kernel(QeQDev e, int token, float *__restrict__ x) {
+__global__ void tk_embed_kernel(QeQDev e, const int *__restrict__ tp, float *__restrict__ x) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= e.cols) return;
+    const int token = tp[0];
     const int ng = e.cols / e.group_size, wpr = e.cols * e.bits / 32;
     const uint32_t *row = e.w + (size_t)token * wpr;
     const size_t g = (size_t)token * ng + c / e.group_size;
@@ -191,12 +192,12 @@ __device__ __forceinline__ void tk_rope_head(float *v, int rot, int pos, float t
 }
 
 /* Per-head RMSNorm of q (from the gated projection, stride 2D) and k, RoPE, and the KV-cache rows of position
- * pos. Blocks 0..Hq-1: q heads; Hq..Hq+Hkv-1: k heads (with their v rows). One warp each. */
+ * pos = tp[1] (the step's token id and position live in device memory, so a captured step replays at any position). Blocks 0..Hq-1: q heads; Hq..Hq+Hkv-1: k heads (with their v rows). One warp each. */
 __global__ void tk_attn_prep_kernel(float *__restrict__ q, const float *__restrict__ qg, float *__restrict__ kc,
                                     float *__restrict__ vc, const float *__restrict__ kx, const float *__restrict__ vx,
                                     const float *__restrict__ q_norm, const float *__restrict__ k_norm, int Hq,
-                                    int Hkv, int D, int rot, int pos, float theta, float eps) {
-    const int blk = blockIdx.x, lane = threadIdx.x;
+                                    int Hkv, int D, int rot, const int *__restrict__ tp, float theta, float eps) {
+    const int blk = blockIdx.x, lane = threadIdx.x, pos = tp[1];
     const bool isq = blk < Hq;
     const int h = isq ? blk : blk - Hq;
     const float *src = isq ? qg + (size_t)h * 2 * D : kx + (size_t)h * D;
@@ -213,14 +214,15 @@ __global__ void tk_attn_prep_kernel(float *__restrict__ q, const float *__restri
         for (int i = lane; i < D; i += 32) vc[((size_t)pos * Hkv + h) * D + i] = vx[(size_t)h * D + i];
 }
 
-/* Causal attention of one query position over positions 0..n-1 for head h (one CTA per head): scores q.k_t / sqrt(D)
+/* Causal attention of one query position over positions 0..n-1 (n = the position in tp[1], plus one) for head h (one CTA per head): scores q.k_t / sqrt(D)
  * (each a sequential sum over D), softmax with the max subtracted and exp and sum in double, o_i = sum_t p_t v_t,i
  * (sequential in t), times sigmoid(gate_i). sc: [Hq][max_len] scratch. */
 __global__ void __launch_bounds__(kNormThreads) tk_attn_kernel(float *__restrict__ att, float *__restrict__ sc,
                                                                const float *__restrict__ q, const float *__restrict__ qg,
                                                                const float *__restrict__ kc,
                                                                const float *__restrict__ vc, int Hq, int Hkv, int D,
-                                                               int n, int max_len) {
+                                                               const int *__restrict__ tp, int max_len) {
+    const int n = tp[1] + 1;
     __shared__ double red[kNormThreads / 32];
     __shared__ float mx_s;
     const int h = blockIdx.x, kvh = h / (Hq / Hkv);
@@ -287,11 +289,18 @@ struct GpuTrunk {
     float *x = nullptr, *h = nullptr, *t1 = nullptr, *t2 = nullptr;
     float *s1 = nullptr, *s2 = nullptr, *s3 = nullptr, *s4 = nullptr, *s5 = nullptr, *sc = nullptr;
     float *logits = nullptr;
+    int *tp = nullptr;                 /* device: the step's token id and position */
+    void *moe_ws = nullptr;            /* the MoE blocks' workspace (private: a captured step keeps its pointers) */
+    int *tp_host = nullptr;            /* pinned host staging of tp */
+    cudaGraphExec_t graph = nullptr;   /* the captured step (after the first eager step) */
+    bool use_graph = true;
     ~GpuTrunk() {
         int cur = 0;
         cudaGetDevice(&cur);
         cudaSetDevice(dev);
         if (s) cudaStreamSynchronize(s);
+        if (graph) cudaGraphExecDestroy(graph);
+        if (tp_host) cudaFreeHost(tp_host);
         for (void *p : allocs) cudaFree(p);
         if (s) cudaStreamDestroy(s);
         cudaSetDevice(cur);
@@ -331,7 +340,10 @@ struct GpuTrunk {
 namespace {
 
 /* y = W x on the device (one token) */
-int tk_matvec(GpuTrunk *t, const QeQDev &m, const float *x, float *y) { return qe_launch_qmatvec(&m, x, 1, y, t->s); }
+int tk_matvec(GpuTrunk *t, const QeQDev &m, const float *x, float *y) {
+    const int rc = qe_launch_dg_matvec(&m, x, y, t->s);   /* the coalesced GEMV, or the general kernel */
+    return rc == 1 ? qe_launch_qmatvec(&m, x, 1, y, t->s) : rc;
+}
 
 int tk_norm(GpuTrunk *t, float *out, const float *x, const float *add, float *hout, const float *w, int n) {
     tk_rmsnorm_kernel<<<1, kNormThreads, 0, t->s>>>(out, x, add, hout, w, n, t->d.eps);
@@ -359,14 +371,14 @@ int tk_gdn(GpuTrunk *t, TkLayerDev &L) {
     return tk_matvec(t, L.out, y, t->t2);
 }
 
-/* Gated full attention on t1 -> t2 at position pos (attn_layer.c; the host trunk's attn_forward) */
-int tk_attn(GpuTrunk *t, TkLayerDev &L, int pos) {
+/* Gated full attention on t1 -> t2 at the step's position (attn_layer.c; the host trunk's attn_forward) */
+int tk_attn(GpuTrunk *t, TkLayerDev &L) {
     const TkDims &d = t->d;
     float *qg = t->s1, *q = t->s2, *att = t->s3, *kx = t->s4, *vx = t->s5;
     if (tk_matvec(t, L.q, t->t1, qg) || tk_matvec(t, L.k, t->t1, kx) || tk_matvec(t, L.v, t->t1, vx)) return -1;
     tk_attn_prep_kernel<<<d.Hq + d.Hkv, 32, 0, t->s>>>(q, qg, L.kc, L.vc, kx, vx, L.q_norm, L.k_norm, d.Hq, d.Hkv, d.D,
-                                                       d.rot, pos, d.theta, d.eps);
-    tk_attn_kernel<<<d.Hq, kNormThreads, 0, t->s>>>(att, t->sc, q, qg, L.kc, L.vc, d.Hq, d.Hkv, d.D, pos + 1, d.max_len);
+                                                       d.rot, t->tp, d.theta, d.eps);
+    tk_attn_kernel<<<d.Hq, kNormThreads, 0, t->s>>>(att, t->sc, q, qg, L.kc, L.vc, d.Hq, d.Hkv, d.D, t->tp, d.max_len);
     QE_CHECK(cudaGetLastError());
     return tk_matvec(t, L.o, att, t->t2);
 }
@@ -414,7 +426,13 @@ GpuTrunk *qe_gtrunk_create(const TkDims &d, const TkHostQ &embed, const TkHostQ 
     ok = ok && (t->x = t->zeros(H)) && (t->h = t->zeros(H)) && (t->t1 = t->zeros(H)) && (t->t2 = t->zeros(H)) &&
          (t->s1 = t->zeros(big)) && (t->s2 = t->zeros(big)) && (t->s3 = t->zeros(big)) &&
          (t->s4 = t->zeros(std::max(big, KVD))) && (t->s5 = t->zeros(std::max((size_t)4 * d.lin_Hv, KVD))) &&
-         (t->sc = t->zeros((size_t)d.Hq * d.max_len)) && (t->logits = t->zeros((size_t)d.vocab));
+         (t->sc = t->zeros((size_t)d.Hq * d.max_len)) && (t->logits = t->zeros((size_t)d.vocab)) &&
+         (t->tp = t->alloc<int>(2)) != nullptr && cudaMallocHost((void **)&t->tp_host, 2 * sizeof(int)) == cudaSuccess;
+    size_t wsb = 0;
+    for (const TkLayerHost &h : layers) wsb = std::max(wsb, qe_moe_ws_bytes(h.moe, 1));
+    ok = ok && wsb > 0 && (t->moe_ws = t->alloc<char>(wsb)) != nullptr;
+    const char *ge = getenv("QE_TRUNK_GRAPH");   /* 0: launch the step's kernels one by one */
+    t->use_graph = !(ge && !strcmp(ge, "0"));
     cudaSetDevice(cur);
     if (!ok) {
         fprintf(stderr, "qengine_b200: GPU trunk: upload failed (%s)\n", cudaGetErrorString(cudaGetLastError()));
@@ -424,31 +442,78 @@ GpuTrunk *qe_gtrunk_create(const TkDims &d, const TkHostQ &embed, const TkHostQ 
     return t;
 }
 
-int qe_gtrunk_forward(GpuTrunk *t, int token, int pos, float *logits) {
+namespace {
+
+/* Enqueue one token's step on t->s (the token id and position already in t->tp); no host work that a graph replay
+ * would skip, except the statistics note when `note` (eager steps). */
+int tk_step(GpuTrunk *t, bool note) {
     const TkDims &d = t->d;
-    if (token < 0 || token >= d.vocab || pos < 0 || pos >= d.max_len) return -1;
-    int cur = 0;
-    cudaGetDevice(&cur);
-    if (cudaSetDevice(t->dev) != cudaSuccess) return -1;
     const int H = d.hidden;
     int rc = 0;
-    tk_embed_kernel<<<(H + 255) / 256, 256, 0, t->s>>>(t->embed, token, t->x);
+    tk_embed_kernel<<<(H + 255) / 256, 256, 0, t->s>>>(t->embed, t->tp, t->x);
     /* per layer (model.c:135-146): x1 = x + mixer(norm(x)); x = x1 + moe(norm(x1)). The residual of the previous
      * layer's MoE block is added inside the next norm (t2 holds that block's output, h its input). */
     for (size_t l = 0; l < t->layers.size() && !rc; l++) {
         TkLayerDev &L = t->layers[l];
         rc = l == 0 ? tk_norm(t, t->t1, t->x, nullptr, nullptr, L.in_norm, H)
                     : tk_norm(t, t->t1, t->h, t->t2, t->x, L.in_norm, H);
-        if (!rc) rc = L.linear ? tk_gdn(t, L) : tk_attn(t, L, pos);
+        if (!rc) rc = L.linear ? tk_gdn(t, L) : tk_attn(t, L);
         if (!rc) rc = tk_norm(t, t->t1, t->x, t->t2, t->h, L.post_norm, H);
-        if (!rc) rc = qe_moe_forward_device(L.moe, 1, t->t1, t->t2, t->s) || qe_moe_note_device_forward(L.moe, 1, t->s);
+        if (!rc) rc = qe_moe_forward_device_ws(L.moe, 1, t->t1, t->t2, t->moe_ws, t->s);
+        if (!rc && note) rc = qe_moe_note_device_forward(L.moe, 1, t->moe_ws, t->s);
     }
     /* the last block's residual, the final norm and the LM head (model.c:150-157) */
     if (!rc) rc = tk_norm(t, t->t1, t->h, t->t2, t->x, t->final_norm, H);
     if (!rc) rc = tk_matvec(t, t->lm_head, t->t1, t->logits);
+    return rc;
+}
+
+/* Capture the step in a CUDA graph (after an eager step has sized every workspace). */
+int tk_capture(GpuTrunk *t) {
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(t->s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return -1;
+    const int rc = tk_step(t, false);
+    const cudaError_t e = cudaStreamEndCapture(t->s, &g);
+    if (rc || e != cudaSuccess || !g) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return -1;
+    }
+    const cudaError_t ie = cudaGraphInstantiate(&t->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) {
+        t->graph = nullptr;
+        cudaGetLastError();
+        return -1;
+    }
+    return 0;
+}
+
+}  // namespace
+
+int qe_gtrunk_forward(GpuTrunk *t, int token, int pos, float *logits) {
+    const TkDims &d = t->d;
+    if (token < 0 || token >= d.vocab || pos < 0 || pos >= d.max_len) return -1;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cudaSetDevice(t->dev) != cudaSuccess) return -1;
+    t->tp_host[0] = token;
+    t->tp_host[1] = pos;
+    int rc = cudaMemcpyAsync(t->tp, t->tp_host, 2 * sizeof(int), cudaMemcpyHostToDevice, t->s) != cudaSuccess;
+    /* QE_TRACE needs each layer's routing read back between the layers: eager steps then */
+    const bool graph = t->use_graph && !getenv("QE_TRACE");
+    if (!rc && graph && t->graph) {
+        rc = cudaGraphLaunch(t->graph, t->s) != cudaSuccess;
+        for (size_t l = 0; l < t->layers.size() && !rc; l++)
+            rc = qe_moe_note_device_forward(t->layers[l].moe, 1, nullptr, nullptr);
+    } else if (!rc) {
+        rc = tk_step(t, true);
+    }
     if (!rc && cudaMemcpyAsync(logits, t->logits, sizeof(float) * d.vocab, cudaMemcpyDeviceToHost, t->s) != cudaSuccess)
         rc = -1;
     if (cudaStreamSynchronize(t->s) != cudaSuccess) rc = -1;
+    /* the first step ran eagerly (and sized the MoE workspaces): capture the step for the next ones */
+    if (!rc && graph && !t->graph && tk_capture(t)) t->use_graph = false;
     cudaSetDevice(cur);
     return rc ? -1 : 0;
 }

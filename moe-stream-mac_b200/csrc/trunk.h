@@ -31,9 +31,12 @@ struct TkLayerHost {
     QeMoe *moe = nullptr;
 };
 
-/* After qe_moe_forward_device inside a caller's own step: read statistics and QE_TRACE records, as
- * qe_moe_forward keeps them (qe_moe.cu). */
-extern "C" int qe_moe_note_device_forward(QeMoe *m, int T, void *stream);
+/* After a device forward inside a caller's own step: read statistics and (with a stream) QE_TRACE records, as
+ * qe_moe_forward keeps them; ws: the workspace the forward used, or null for the device's shared one. And the
+ * device forward on a caller's workspace (qe_moe_ws_bytes(m, T) bytes), stable under graph capture (qe_moe.cu). */
+extern "C" int qe_moe_note_device_forward(QeMoe *m, int T, void *ws, void *stream);
+extern "C" size_t qe_moe_ws_bytes(const QeMoe *m, int T);
+extern "C" int qe_moe_forward_device_ws(QeMoe *m, int T, const float *x, float *out, void *ws, void *stream);
 
 struct GpuTrunk;
 /* Upload the trunk to CUDA device `dev` (the MoE handles' device). NULL on failure (reason on stderr). */

@@ -118,3 +118,36 @@ def test_engine_context_full_and_bad_token(tmp_path):
         assert lib.qe_forward(h, 4, p) == 0
     finally:
         lib.qe_free(h)
+
+
+def test_engine_trace_records_every_layer(tmp_path):
+    """QE_TRACE through the whole-model API (moe_layer.c:57-64: int32 layer id, then the top-k expert ids, per token and
+    layer): the GPU trunk's steps write one record per MoE block and token, layers in order, ids valid and distinct."""
+    d = tmp_path / "model"
+    m = write_tiny_model(d, TinyModel(), seed=11)
+    trace = tmp_path / "trace.bin"
+    code = r"""
+import ctypes as C, os, sys
+import numpy as np
+sys.path[:0] = sys.argv[3:]
+import qmoe
+from test_engine_cpu import _qchat_bind
+lib = _qchat_bind(qmoe.LIB_PATH)
+h = lib.qe_load(sys.argv[1].encode(), 8)
+assert h
+lg = np.zeros(int(sys.argv[2]), np.float32)
+for t in (3, 9, 27, 81):
+    assert lib.qe_forward(h, t, lg.ctypes.data_as(C.POINTER(C.c_float))) == 0
+lib.qe_free(h)
+"""
+    env = dict(__import__("os").environ, QE_TRACE=str(trace), QE_TRUNK="gpu")
+    r = subprocess.run([sys.executable, "-c", code, str(d), str(m.vocab), str(REPO / "tests"),
+                        str(REPO / "moe-stream-mac_b200"), str(REPO)], capture_output=True, text=True, env=env,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr
+    rec = np.fromfile(trace, np.int32).reshape(-1, 1 + m.top_k)
+    assert rec.shape[0] == 4 * m.n_layers
+    assert np.array_equal(rec[:, 0], np.tile(np.arange(m.n_layers), 4))
+    ids = rec[:, 1:]
+    assert ids.min() >= 0 and ids.max() < m.E
+    assert all(len(set(row)) == m.top_k for row in ids.tolist())

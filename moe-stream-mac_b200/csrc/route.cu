@@ -664,7 +664,8 @@ int qe_launch_router_f32(const float *W, const float *bias, const float *x, int 
     if (H > 32 * kMaxLaneChunks * kChunk) QE_FAIL("router: hidden %d too large", H);
     int launches = 1;
     if (T <= 16) {
-        const int rows = E + 1, warps_per_block = 4;
+        /* one warp (router row) per CTA: every SM streams router rows (4 per CTA left 83 of 148 SMs idle) */
+        const int rows = E + 1, warps_per_block = 1;
         const int vec = H % 4 == 0 && ((uintptr_t)W | (uintptr_t)x) % 16 == 0;
         router_gemv_f32_kernel<<<(rows + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, s>>>(
             W, bias, x, T, H, E, logits, vec);

@@ -72,6 +72,7 @@ __device__ __forceinline__ void router_row_f32(const float *__restrict__ W, cons
                 if (cc * 32 + src >= nch) break;
 #pragma unroll
                 for (int t = 0; t < kRouterGemvTokens; t++) {
+                    if (t >= nt) break;   /* nt is the same for the whole warp: no shuffle for absent tokens */
                     const float v = __shfl_sync(QE_FULL, acc[cc][t], src);
                     total[t] = __fadd_rn(total[t], v);
                 }

@@ -6,9 +6,10 @@
  * partial RoPE and an fp32 KV cache; model.c:135-157 the layer and model steps), as the host trunk of engine.cu
  * implements them. Element-wise arithmetic keeps the host trunk's fp32 operation order (separate multiplies and
  * adds, sequential sums where the host sums sequentially); norms and the attention softmax sum in double, with a
- * fixed tree order in place of the host's left-to-right order. The quantized projections and the LM head are
- * this library's GPU matrix-vector kernel (qe_launch_qmatvec, qmat.c:36-46 semantics). Everything of a token
- * stays on the device; the logits are the only copy back.
+ * fixed tree order in place of the host's left-to-right order. The quantized projections and the LM head run on
+ * the decode path's coalesced GEMV (qe_launch_dg_matvec; the general qe_launch_qmatvec for other shapes), with
+ * qmat.c:36-46 semantics. Everything of a token stays on the device, and after the first step the whole step is
+ * replayed from a CUDA graph; the logits are the only copy back.
  */
 #include <math.h>
 #include <stdio.h>

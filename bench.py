@@ -276,16 +276,18 @@ def profiled_traffic(kernel: str, config: str):
 
 
 def expert_kernel_name(cfg, stage: str, T: int) -> str:
-    """The kernel the library runs for this stage: decode GEMVs for up to 4 tokens, the tensor-core kernels for
-    larger batches (group size 64, every matrix a whole number of 128-row tiles), the grouped GEMVs when
-    selected (QE_EXPERT_PATH=group), mma.sync kernels otherwise."""
+    """The kernel the library runs for this stage: decode GEMVs for up to 4 tokens, the grouped GEMVs for larger
+    batches of at most 4 routed assignments per expert on average (or when selected, QE_EXPERT_PATH=group), the
+    tensor-core kernels for the rest (group size 64, every matrix a whole number of 128-row tiles), mma.sync
+    kernels otherwise."""
     path = os.environ.get("QE_EXPERT_PATH", "auto")
     bh, bi = cfg.hidden * cfg.bits // 8, cfg.inter * cfg.bits // 8
     tc = (T >= 5 and cfg.group_size == 64 and all(d % 128 == 0 for d in (cfg.hidden, cfg.inter, cfg.sh_inter))
           and path in ("auto", "tc"))
     decode = (T <= 4 and cfg.group_size == 64 and cfg.inter == cfg.sh_inter and path in ("auto", "gemv")
               and bh % 128 == 0 and bh // 128 >= 8 and bi % 128 == 0)
-    group = path == "group" and cfg.group_size == 64 and bh % 64 == 0 and bh // 64 >= 4 and bi % 64 == 0
+    group = ((path == "group" or (path == "auto" and 4 < T and T * cfg.top_k <= 4 * cfg.E))
+             and cfg.bits in (4, 8) and cfg.group_size == 64)
     if decode:
         def coalesced(K: int, slots: int, max_warps: int) -> bool:
             # the library's choice (decode.cu dg_supported): 16-byte lanes, a power of two (2..16) per row or
@@ -300,7 +302,7 @@ def expert_kernel_name(cfg, stage: str, T: int) -> str:
         return (f"dg_down_kernel<{cfg.bits}>" if coalesced(cfg.inter, cfg.top_k + 1, 18)
                 else f"decode_down_combine_kernel<{cfg.bits}>")
     if group:
-        return f"group_gateup_kernel<{cfg.bits}>" if stage == "gateup" else f"group_down_kernel<{cfg.bits}>"
+        return f"gm_kernel<{cfg.bits},{'true' if stage == 'gateup' else 'false'}>"
     if tc:
         return f"tc_expert_kernel<{cfg.bits},{2 if stage == 'gateup' else 1}>"
     return f"expert_kernel<{cfg.bits},{cfg.group_size},{stage}>"

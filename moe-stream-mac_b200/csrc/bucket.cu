@@ -100,6 +100,16 @@ __global__ void __launch_bounds__(kThreads) bucket_kernel(const int32_t *__restr
         if (lane == 0) cdn[na] = tot;
     }
     __syncthreads();
+    /* with one gate/up tile per expert, the items are the chunks themselves: list them (at most one per pair) */
+    if (b.chunks && tiles_gu == 1 && tiles_sh_gu == 1) {
+        for (int e = tid; e <= E; e += kThreads) {
+            const int n = cnt[e];
+            if (n == 0) continue;
+            const int base = cgu[flag[e]];
+            for (int c = 0, n0 = 0; n0 < n; c++, n0 += chunk)
+                b.chunks[base + c] = make_int4(e, off[e] + n0, min(chunk, n - n0), 0);
+        }
+    }
     for (int a = tid; a <= na; a += kThreads) {
         b.slot_items[a] = cgu[a];
         b.slot_items[(E + 2) + a] = cdn[a];

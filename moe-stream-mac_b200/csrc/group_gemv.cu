@@ -1,21 +1,31 @@
-/* group_gemv.cu: the expert stage of a batched decode step (a few tokens per expert) as expert-centric
- * CUDA-core GEMVs.
+/* group_gemv.cu: the expert stage of a batched decode step (a few tokens per expert) as expert-centric GEMVs on
+ * mma.sync tensor-core fragments.
  *
  * Reference: engine/src/moe_layer.c:20-26 (mlp: gate, up, silu*up, down), engine/src/qmat.c:15-49 (per row,
- * per group of 64: scale*sum(q*x) + bias*sum(x)), engine/src/qgroup.c (code j of a group at bit
- * (j % (32/bits))*bits of word j / (32/bits), LSB first). The reference runs one token at a time; here the
- * tokens of a batch are bucketed by expert (bucket.cu) and every active expert's rows are streamed from HBM
- * once per chunk of up to kNT of its tokens, each code converted once and dotted with all of them.
+ * per group of 64: scale*sum(q*x) + bias*sum(x)), engine/src/qgroup.c (code j of a group at bit (j % (32/bits))*bits
+ * of word j / (32/bits), LSB first). The reference runs one token at a time; here the tokens of a batch are
+ * bucketed by expert (bucket.cu, which also lists each expert's tokens in chunks of up to 4) and every active
+ * expert's rows are streamed from HBM once per chunk.
  *
- *   group_gateup_kernel  CTA = (expert, chunk of <= kNT tokens, 32 rows); warps 0-3 stream the gate rows,
- *                        4-7 the up rows, each warp a quarter of K, one lane per row; parts summed in order,
- *                        h = silu(g) * u per (token, row) -> h3[pair][row]
- *   group_down_kernel    CTA = (expert, chunk, 32 output rows); 4 warps split K; y -> ybuf[pair][row], summed
- *                        per token by the combine kernel in slot order
- * A lane streams its row in 64-byte chunks (4 x 16-byte loads; the warp's 32 rows are 32 such streams) through
- * a 2-deep register ring with the chunk's scales and biases; the first loads are issued before the tokens'
- * vectors are staged in shared memory (reads there are broadcasts). Codes are formed as 1 + q/2^b floats and
- * the group sum of x subtracted, as in decode.cu; fp32 throughout (tolerance 1e-5 rel-L2).
+ * At ~2 tokens per expert (64-token batched decode over 256 experts) the stage is the weight stream, and on CUDA
+ * cores its cost is the code conversion and one FMA per code and token. Here one warp-wide mma.m16n8k16 takes 16
+ * rows x 16 codes against 8 columns: the hi and lo fp16 terms of up to 4 tokens (the activations split per group
+ * of 64 as for the tcgen05 kernels: v * 2^e = hi + lo, expert_tc.cu), so a code costs about one conversion
+ * instruction whatever the chunk's token count:
+ *   item       (chunk of <= 4 tokens, tile of 16 rows), one warp, walked by a persistent grid of warps; the warp
+ *              streams its rows' codes over the whole K (gate and up together for gate/up)
+ *   fragments  thread (g, c) = (lane / 4, lane % 4) loads 16 consecutive codes of rows g and g + 8 per group and
+ *              feeds them to the 4 MMAs of the group as the k pairs {2c, 2c+1} and {2c+8, 2c+9}; the activation
+ *              rows are laid out so that column n = (token n / 2, term n % 2) holds the same inputs at the same
+ *              fragment slots (natural order for 8-bit codes, the nibble pairs (i, i+4) of each word for 4-bit)
+ *   conversion a code pair becomes the fp16 pair (1024 + q0, 1024 + q1) by one byte permute (8-bit) or one logic
+ *              op (4-bit), and one paired subtraction leaves (q0, q1): exact
+ *   epilogue   per group, fp32 in registers as the reference: acc += scale * (hi + lo) * 2^-e + bias * sum(x), the
+ *              tensor core's own accumulation limited to the 4 k16 steps of a group
+ *   gate/up    h = silu(g) * u (ops.c:16-21) -> h3[pair][row] (fp32; split for the down projection by
+ *              qe_launch_split_rows)
+ *   down       y -> ybuf[pair][row], summed per token by the combine kernel in slot order (moe_layer.c:79-88)
+ * The next group's codes, activations, scales and biases are loaded while this group's MMAs run.
  */
 #include "qe_common.cuh"
 #include "qe_kernels.h"
@@ -23,329 +33,230 @@
 namespace {
 
 constexpr int kGS = 64;
-constexpr int kNT = 4;                 /* tokens per chunk */
-constexpr int kChunk = 64;             /* bytes a lane loads per ring slot */
-constexpr int kU4 = kChunk / 16;
-constexpr int kGuParts = 4;            /* K parts per matrix, gate/up kernel */
-constexpr int kDnParts = 4;            /* K parts, down kernel */
+constexpr int kTok = 4;                /* tokens per chunk: the MMA's 8 columns hold their hi and lo terms */
+constexpr int kWarps = 8;              /* warps per CTA (each walks its own items) */
 
-/* Code I of word w as the float 1 + q/2^b: the code's bits become the top mantissa bits. */
-template <int BITS, int I>
-__device__ __forceinline__ float code_v(uint32_t w) {
-    constexpr int kTop = 23 - BITS;
-    constexpr int kSh = kTop - BITS * I;
-    constexpr uint32_t kMask = ((1u << BITS) - 1u) << kTop;
-    const uint32_t s = kSh >= 0 ? (w << (kSh >= 0 ? kSh : 0)) : (w >> (kSh < 0 ? -kSh : 0));
-    return __uint_as_float((s & kMask) | 0x3F800000u);
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-/* One lane's row: chunks [c0, c1) of codes with their groups' scales and biases, a 2-deep register ring. */
+/* (1024 + q0, 1024 + q1) - (1024, 1024) = (q0, q1) as an fp16 pair: exact for codes below 2^11. */
+__device__ __forceinline__ uint32_t h2_sub1024(uint32_t v) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(0x64006400u));
+    return r;
+}
+
+/* The fp16 code pairs of one 32-bit word, in the order the activation layout expects:
+ * 8-bit: (q0, q1), (q2, q3); 4-bit: (n0, n4), (n1, n5), (n2, n6), (n3, n7). */
 template <int BITS>
-struct Stream {
-    static constexpr int GB = 64 * BITS / 8;        /* bytes per group */
-    static constexpr int GPC = kChunk / GB;         /* groups per chunk */
-    const uint8_t *row;
-    const uint16_t *sc, *bi;
-    size_t gstride;
-    int c0, c1;
-    uint4 w[2][kU4];
-    uint32_t sb[2][GPC];
-
-    __device__ __forceinline__ void load(int slot, int c) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(row + (size_t)c * kChunk);
-#pragma unroll
-        for (int i = 0; i < kU4; i++) w[slot][i] = __ldg(p + i);
-#pragma unroll
-        for (int gi = 0; gi < GPC; gi++) {
-            const size_t g = (size_t)(c * GPC + gi) * gstride;
-            sb[slot][gi] = (uint32_t)__ldg(sc + g) | ((uint32_t)__ldg(bi + g) << 16);
-        }
-    }
-    __device__ __forceinline__ void start() {
-        if (c0 < c1) load(0, c0);
-        if (c0 + 1 < c1) load(1, c0 + 1);
-    }
-    /* acc[n] += scale*sum_q + bias*sum_x over the chunk's groups (group order), for the nt vectors
-     * xs[n*ldx ..] with group sums gs[n*ldg ..] */
-    __device__ __forceinline__ void chunk(int slot, int c, const float *xs, int ldx, const float *gs, int ldg, int nt,
-                                          float (&acc)[kNT]) const {
-#pragma unroll
-        for (int gi = 0; gi < GPC; gi++) {
-            const int g = c * GPC + gi;
-            float2 a[kNT];
-#pragma unroll
-            for (int n = 0; n < kNT; n++) a[n] = make_float2(0.0f, 0.0f);
-#pragma unroll
-            for (int i = 0; i < GB / 16; i++) {
-                const uint4 wv = w[slot][gi * (GB / 16) + i];
-                const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
-                const int k0 = g * 64 + i * (128 / BITS);   /* first input of this 16-byte word */
-#pragma unroll
-                for (int qd = 0; qd < 4; qd++) {
-                    constexpr int CPW = 32 / BITS;          /* codes per 32-bit word */
-                    float2 cv[CPW / 2];
-#pragma unroll
-                    for (int h = 0; h < CPW / 2; h++) {
-                        if constexpr (BITS == 4) {
-                            const uint32_t x = ws[qd];
-                            cv[h] = make_float2(h == 0 ? code_v<4, 0>(x) : h == 1 ? code_v<4, 2>(x) : h == 2 ? code_v<4, 4>(x) : code_v<4, 6>(x),
-                                                h == 0 ? code_v<4, 1>(x) : h == 1 ? code_v<4, 3>(x) : h == 2 ? code_v<4, 5>(x) : code_v<4, 7>(x));
-                        } else {
-                            const uint32_t x = ws[qd];
-                            cv[h] = make_float2(h == 0 ? code_v<8, 0>(x) : code_v<8, 2>(x),
-                                                h == 0 ? code_v<8, 1>(x) : code_v<8, 3>(x));
-                        }
-                    }
-#pragma unroll
-                    for (int n = 0; n < kNT; n++) {
-                        if (n < nt) {
-                            const float4 *x4 = reinterpret_cast<const float4 *>(xs + (size_t)n * ldx + k0 + qd * CPW);
-#pragma unroll
-                            for (int h = 0; h < CPW / 4; h++) {
-                                const float4 xv = x4[h];
-                                a[n] = __ffma2_rn(cv[2 * h], make_float2(xv.x, xv.y), a[n]);
-                                a[n] = __ffma2_rn(cv[2 * h + 1], make_float2(xv.z, xv.w), a[n]);
-                            }
-                        }
-                    }
-                }
-            }
-            const float s = __uint_as_float(sb[slot][gi] << 16), b = __uint_as_float(sb[slot][gi] & 0xFFFF0000u);
-#pragma unroll
-            for (int n = 0; n < kNT; n++) {
-                if (n < nt) {
-                    const float gsum = gs[(size_t)n * ldg + g];
-                    const float sq = __fmul_rn(__fsub_rn(__fadd_rn(a[n].x, a[n].y), gsum), (float)(1 << BITS));
-                    acc[n] = __fadd_rn(acc[n], __fmaf_rn(s, sq, __fmul_rn(b, gsum)));
-                }
-            }
-        }
-    }
-    __device__ __forceinline__ void finish(const float *xs, int ldx, const float *gs, int ldg, int nt,
-                                           float (&acc)[kNT]) {
-        for (int c = c0; c < c1; c += 2) {
-            chunk(0, c, xs, ldx, gs, ldg, nt, acc);
-            if (c + 2 < c1) load(0, c + 2);
-            if (c + 1 < c1) {
-                chunk(1, c + 1, xs, ldx, gs, ldg, nt, acc);
-                if (c + 3 < c1) load(1, c + 3);
-            }
-        }
-    }
-};
-
-/* The quantized matrix (routed expert e, or the shared one) as row pointers. */
-struct QRow {
-    const uint8_t *codes;
-    const uint16_t *sc, *bi;
-    size_t gstride;
-};
-__device__ __forceinline__ QRow qrow(const QeQDev &m, int e, int row) {
-    const int ng = m.cols / kGS;
-    const size_t bpr = (size_t)m.cols * m.bits / 8;
-    QRow q;
-    q.codes = reinterpret_cast<const uint8_t *>(m.w) + ((size_t)e * m.rows + row) * bpr;
-    if (m.scale_t) {
-        const size_t o = (size_t)e * ng * m.rows + row;
-        q.sc = m.scales + o;
-        q.bi = m.biases + o;
-        q.gstride = m.rows;
+__device__ __forceinline__ void code_pairs(uint32_t w, uint32_t (&p)[16 / BITS]) {
+    if constexpr (BITS == 8) {
+        p[0] = h2_sub1024(__byte_perm(w, 0x64646464u, 0x4140));
+        p[1] = h2_sub1024(__byte_perm(w, 0x64646464u, 0x4342));
     } else {
-        const size_t o = ((size_t)e * m.rows + row) * ng;
-        q.sc = m.scales + o;
-        q.bi = m.biases + o;
-        q.gstride = 1;
-    }
-    return q;
-}
-
-/* n vectors of K floats into shared memory (vs[j*K + c]) and their sums per group of 64 (gs[j*(K/64) + g]):
- * one warp per group, lanes add pairs, then a fixed shuffle tree. */
-template <typename Src>
-__device__ void stage_vecs(Src src, int n, int K, float *vs, float *gs) {
-    for (int i = threadIdx.x; i < n * (K / 4); i += blockDim.x) {
-        const int j = i / (K / 4), c = i % (K / 4);
-        reinterpret_cast<float4 *>(vs + (size_t)j * K)[c] = reinterpret_cast<const float4 *>(src(j))[c];
-    }
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5, ng = K / kGS;
-    for (int i = warp; i < n * ng; i += nw) {
-        const float *v = vs + (size_t)(i / ng) * K + (size_t)(i % ng) * kGS;
-        float s = __fadd_rn(v[2 * lane], v[2 * lane + 1]);
 #pragma unroll
-        for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(QE_FULL, s, o));
-        if (lane == 0) gs[i] = s;
+        for (int i = 0; i < 4; i++) p[i] = h2_sub1024(((w >> (4 * i)) & 0x000F000Fu) | 0x64006400u);
     }
-    __syncthreads();
 }
 
-struct GItem {
-    int e, off, n0, nt, r0;
-    bool shared;
+/* A thread's share of one group of a row: 16 codes (16 bytes for 8-bit, 8 bytes for 4-bit). */
+template <int BITS> struct Codes;
+template <> struct Codes<8> {
+    uint4 v;
+    __device__ __forceinline__ void load(const uint8_t *p) { v = __ldg(reinterpret_cast<const uint4 *>(p)); }
+    __device__ __forceinline__ uint32_t word(int i) const { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+};
+template <> struct Codes<4> {
+    uint2 v;
+    __device__ __forceinline__ void load(const uint8_t *p) { v = __ldg(reinterpret_cast<const uint2 *>(p)); }
+    __device__ __forceinline__ uint32_t word(int i) const { return i == 0 ? v.x : v.y; }
 };
 
-/* Work item -> (expert, token chunk, 32-row tile), from the bucket lists (same decomposition as the
- * tensor-core kernels: items of a slot are tile-major, chunk-minor). */
-__device__ __forceinline__ GItem gitem(const QeBuckets &b, const int32_t *prefix, int na, int E, int item) {
-    int lo = 0, hi = na;
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (prefix[mid] <= item) lo = mid; else hi = mid;
+/* The A fragments of MMA s (0..3) of a group from the codes of rows g (r0) and g + 8 (r8). */
+template <int BITS>
+__device__ __forceinline__ void a_frag(const Codes<BITS> &r0, const Codes<BITS> &r8, int s, uint32_t (&a)[4]) {
+    if constexpr (BITS == 8) {      /* MMA s: bytes 4s .. 4s + 3 = word s */
+        uint32_t p0[2], p8[2];
+        code_pairs<8>(r0.word(s), p0);
+        code_pairs<8>(r8.word(s), p8);
+        a[0] = p0[0]; a[1] = p8[0]; a[2] = p0[1]; a[3] = p8[1];
+    } else {                        /* MMA s: pairs 2(s%2), 2(s%2)+1 of word s/2 */
+        const uint32_t w0 = r0.word(s >> 1) >> (8 * (s & 1)), w8 = r8.word(s >> 1) >> (8 * (s & 1));
+        a[0] = h2_sub1024((w0 & 0x000F000Fu) | 0x64006400u);
+        a[1] = h2_sub1024((w8 & 0x000F000Fu) | 0x64006400u);
+        a[2] = h2_sub1024(((w0 >> 4) & 0x000F000Fu) | 0x64006400u);
+        a[3] = h2_sub1024(((w8 >> 4) & 0x000F000Fu) | 0x64006400u);
     }
-    GItem it;
-    it.e = b.slot_expert[lo];
-    it.shared = it.e == E;
-    const int cnt = b.counts[it.e];
-    it.off = b.offsets[it.e];
-    const int ntn = (cnt + kNT - 1) / kNT;
-    const int local = item - prefix[lo];
-    it.r0 = (local / ntn) * 32;
-    it.n0 = (local % ntn) * kNT;
-    it.nt = min(kNT, cnt - it.n0);
-    return it;
 }
 
-template <int BITS>
-__global__ void __launch_bounds__(2 * kGuParts * 32, 2) group_gateup_kernel(QeExpertArgs a, const float *__restrict__ x,
-                                                                            QeBuckets b, int kp1,
-                                                                            float *__restrict__ h3, int ldh) {
-    extern __shared__ __align__(16) float smem[];
-    __shared__ float part[2 * kGuParts][kNT][32];
-    const int na = b.n_active[0], nitems = b.n_active[1];
-    for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
-    const GItem it = gitem(b, b.slot_items, na, a.E, item);
-    const QeQDev &G = it.shared ? a.sh_gate : a.gate, &U = it.shared ? a.sh_up : a.up;
-    const int rows = G.rows, K = G.cols, e = it.shared ? 0 : it.e;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m = warp / kGuParts, pt = warp % kGuParts;
-    const int row = min(it.r0 + lane, rows - 1);
-    const int nch = K * BITS / 8 / kChunk;
-    const QRow q = qrow(m ? U : G, e, row);
-    Stream<BITS> st;
-    st.row = q.codes; st.sc = q.sc; st.bi = q.bi; st.gstride = q.gstride;
-    st.c0 = pt * nch / kGuParts;
-    st.c1 = (pt + 1) * nch / kGuParts;
-    st.start();                               /* codes in flight while the tokens' vectors are staged */
-    float *xs = smem, *gs = smem + (size_t)kNT * K;
-    stage_vecs([&](int j) { return x + (size_t)(b.pairs[it.off + it.n0 + j] / kp1) * K; }, it.nt, K, xs, gs);
-    float acc[kNT];
+/* Everything one group step reads besides the codes: this thread's activation words (B fragments for the 4
+ * MMAs), the scales and biases of its two rows, and its D-column token's unscale factor and group sum. */
+struct GroupIn {
+    uint4 b0, b1;          /* 8 fp16 pairs: MMA s takes (b0/b1 word 2s, 2s+1) */
+    uint32_t sb0[2], sb8[2];   /* per matrix: scale | bias << 16 of rows g and g + 8 */
+    float f, xs;
+};
+
+template <int BITS, bool GU>
+__global__ void __launch_bounds__(kWarps * 32) gm_kernel(QeExpertArgs a, const __half *__restrict__ act, int arows,
+                                                         int lda, const float *__restrict__ asum,
+                                                         const float *__restrict__ ainv, int ldg_s, QeBuckets b,
+                                                         int div, float *__restrict__ dst, int ldd) {
+    constexpr int NM = GU ? 2 : 1;
+    constexpr int GB = kGS * BITS / 8;                   /* bytes of a group in a row */
+    const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+    const int rows_max = GU ? max(a.gate.rows, a.sh_gate.rows) : a.hidden;
+    const int ntiles = (rows_max + 15) / 16, nch = b.n_active[1];
+    const int items = nch * ntiles, nwarps = gridDim.x * kWarps;
+    for (int item = blockIdx.x * kWarps + (threadIdx.x >> 5); item < items; item += nwarps) {
+        const int4 ch = b.chunks[item / ntiles];         /* expert, first bucket position, tokens */
+        const bool sh = ch.x == a.E;
+        const int e = sh ? 0 : ch.x, nt = ch.z;
+        const QeQDev M0 = GU ? (sh ? a.sh_gate : a.gate) : (sh ? a.sh_down : a.down);
+        const QeQDev M1 = GU ? (sh ? a.sh_up : a.up) : M0;
+        const int rows = M0.rows, r0 = (item % ntiles) * 16;
+        if (r0 >= rows) continue;                        /* uniform over the warp */
+        const int K = M0.cols, ng = K / kGS;
+        const int rg = r0 + g, rg8 = min(r0 + g + 8, rows - 1);   /* rows are a multiple of 8 */
+        /* B: column g = (token g / 2, term g % 2), inputs 16c .. 16c + 15 of each group */
+        const int tb = g >> 1;
+        const bool bon = tb < nt;
+        const int brow = bon ? b.pairs[ch.y + tb] / div : 0;
+        const __half *bp = act + ((size_t)(g & 1) * arows + brow) * lda + 16 * c;
+        /* D columns 2c, 2c + 1: token c's hi and lo */
+        const bool don = c < nt;
+        const int drow = don ? b.pairs[ch.y + c] / div : 0;
+        const float *fp = ainv + (size_t)drow * ldg_s, *sp = asum + (size_t)drow * ldg_s;
+        const size_t bpr = (size_t)K * BITS / 8;
+        const uint8_t *c0[NM], *c8[NM];
+        const uint16_t *sc[NM], *bi[NM];
 #pragma unroll
-    for (int n = 0; n < kNT; n++) acc[n] = 0.0f;
-    st.finish(xs, K, gs, K / kGS, it.nt, acc);
-#pragma unroll
-    for (int n = 0; n < kNT; n++) part[warp][n][lane] = acc[n];
-    __syncthreads();
-    /* thread (n, lane): token n of the chunk, row r0 + lane; parts summed in order, then SwiGLU (ops.c:16-21) */
-    const int n = threadIdx.x >> 5;
-    if (n < it.nt && it.r0 + lane < rows) {
-        float g = 0.0f, u = 0.0f;
-        for (int i = 0; i < kGuParts; i++) {
-            g = __fadd_rn(g, part[i][n][lane]);
-            u = __fadd_rn(u, part[kGuParts + i][n][lane]);
+        for (int mi = 0; mi < NM; mi++) {
+            const QeQDev &M = mi ? M1 : M0;
+            const uint8_t *base = reinterpret_cast<const uint8_t *>(M.w) + (size_t)e * rows * bpr + (size_t)c * (GB / 4);
+            c0[mi] = base + (size_t)rg * bpr;
+            c8[mi] = base + (size_t)rg8 * bpr;
+            sc[mi] = M.scales + (size_t)e * ng * rows;   /* [expert][group][row] */
+            bi[mi] = M.biases + (size_t)e * ng * rows;
         }
-        const int pid = b.pairs[it.off + it.n0 + n];
-        h3[(size_t)pid * ldh + it.r0 + lane] = qe_silu_mul(g, u);
-    }
-    __syncthreads();   /* shared memory is restaged by the next item */
+        auto load = [&](int gi, Codes<BITS> (&w0)[NM], Codes<BITS> (&w8)[NM], GroupIn &in) {
+#pragma unroll
+            for (int mi = 0; mi < NM; mi++) {
+                w0[mi].load(c0[mi] + (size_t)gi * GB);
+                w8[mi].load(c8[mi] + (size_t)gi * GB);
+                const size_t o = (size_t)gi * rows;
+                in.sb0[mi] = (uint32_t)__ldg(sc[mi] + o + rg) | ((uint32_t)__ldg(bi[mi] + o + rg) << 16);
+                in.sb8[mi] = (uint32_t)__ldg(sc[mi] + o + rg8) | ((uint32_t)__ldg(bi[mi] + o + rg8) << 16);
+            }
+            if (bon) {
+                const uint4 *q = reinterpret_cast<const uint4 *>(bp + (size_t)gi * kGS);
+                in.b0 = __ldg(q);
+                in.b1 = __ldg(q + 1);
+            } else {
+                in.b0 = in.b1 = make_uint4(0u, 0u, 0u, 0u);
+            }
+            in.f = don ? __ldg(fp + gi) : 0.0f;
+            in.xs = don ? __ldg(sp + gi) : 0.0f;
+        };
+        float acc[NM][2];
+#pragma unroll
+        for (int mi = 0; mi < NM; mi++) acc[mi][0] = acc[mi][1] = 0.0f;
+        Codes<BITS> w0[2][NM], w8[2][NM];
+        GroupIn in[2];
+        load(0, w0[0], w8[0], in[0]);
+        /* two groups per iteration, so the double buffer is indexed by constants */
+        for (int gi = 0; gi < ng; gi += 2) {
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                if (gi + u >= ng) break;
+                if (gi + u + 1 < ng) load(gi + u + 1, w0[u ^ 1], w8[u ^ 1], in[u ^ 1]);
+                const uint32_t bw[8] = {in[u].b0.x, in[u].b0.y, in[u].b0.z, in[u].b0.w,
+                                        in[u].b1.x, in[u].b1.y, in[u].b1.z, in[u].b1.w};
+#pragma unroll
+                for (int mi = 0; mi < NM; mi++) {
+                    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                    for (int s = 0; s < 4; s++) {
+                        uint32_t af[4];
+                        a_frag<BITS>(w0[u][mi], w8[u][mi], s, af);
+                        mma16816(d, af[0], af[1], af[2], af[3], bw[2 * s], bw[2 * s + 1]);
+                    }
+                    /* rows g and g + 8, token c: (hi + lo) * 2^-e, then scale and bias (qmat.c:43) */
+                    const float p0 = __fmul_rn(__fadd_rn(d[0], d[1]), in[u].f);
+                    const float p8 = __fmul_rn(__fadd_rn(d[2], d[3]), in[u].f);
+                    const uint32_t s0 = in[u].sb0[mi], s8 = in[u].sb8[mi];
+                    acc[mi][0] = __fadd_rn(acc[mi][0], __fmaf_rn(__uint_as_float(s0 << 16), p0,
+                                                                __fmul_rn(__uint_as_float(s0 & 0xFFFF0000u), in[u].xs)));
+                    acc[mi][1] = __fadd_rn(acc[mi][1], __fmaf_rn(__uint_as_float(s8 << 16), p8,
+                                                                __fmul_rn(__uint_as_float(s8 & 0xFFFF0000u), in[u].xs)));
+                }
+            }
+        }
+        if (don) {
+            const int pid = b.pairs[ch.y + c];
+            float y0 = acc[0][0], y8 = acc[0][1];
+            if constexpr (GU) {
+                y0 = qe_silu_mul(acc[0][0], acc[NM - 1][0]);
+                y8 = qe_silu_mul(acc[0][1], acc[NM - 1][1]);
+            }
+            dst[(size_t)pid * ldd + rg] = y0;
+            if (r0 + g + 8 < rows) dst[(size_t)pid * ldd + r0 + g + 8] = y8;
+        }
     }
 }
 
-template <int BITS>
-__global__ void __launch_bounds__(kDnParts * 32) group_down_kernel(QeExpertArgs a, const float *__restrict__ h3,
-                                                                   int ldh, QeBuckets b, float *__restrict__ ybuf) {
-    extern __shared__ __align__(16) float smem[];
-    __shared__ float part[kDnParts][kNT][32];
-    const int na = b.n_active[0], nitems = b.n_active[2];
-    for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
-    const GItem it = gitem(b, b.slot_items + (a.E + 2), na, a.E, item);
-    const QeQDev &D = it.shared ? a.sh_down : a.down;
-    const int H = D.rows, K = D.cols, e = it.shared ? 0 : it.e;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = min(it.r0 + lane, H - 1);
-    const int nch = K * BITS / 8 / kChunk;
-    const QRow q = qrow(D, e, row);
-    Stream<BITS> st;
-    st.row = q.codes; st.sc = q.sc; st.bi = q.bi; st.gstride = q.gstride;
-    st.c0 = warp * nch / kDnParts;
-    st.c1 = (warp + 1) * nch / kDnParts;
-    st.start();
-    float *hs = smem, *gs = smem + (size_t)kNT * K;
-    stage_vecs([&](int j) { return h3 + (size_t)b.pairs[it.off + it.n0 + j] * ldh; }, it.nt, K, hs, gs);
-    float acc[kNT];
-#pragma unroll
-    for (int n = 0; n < kNT; n++) acc[n] = 0.0f;
-    st.finish(hs, K, gs, K / kGS, it.nt, acc);
-#pragma unroll
-    for (int n = 0; n < kNT; n++) part[warp][n][lane] = acc[n];
-    __syncthreads();
-    for (int n = warp; n < it.nt; n += kDnParts) {
-        if (it.r0 + lane >= H) continue;
-        float y = 0.0f;
-        for (int i = 0; i < kDnParts; i++) y = __fadd_rn(y, part[i][n][lane]);
-        ybuf[(size_t)b.pairs[it.off + it.n0 + n] * H + it.r0 + lane] = y;
-    }
-    __syncthreads();   /* shared memory is restaged by the next item */
-    }
+template <int BITS, bool GU>
+int launch(const QeExpertArgs *a, const __half *act, int arows, int lda, const float *asum, const float *ainv,
+           int ldg_s, const QeBuckets *b, int div, float *dst, int ldd, int sms, cudaStream_t s) {
+    const void *k = (const void *)gm_kernel<BITS, GU>;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kWarps * 32, 0) != cudaSuccess || n < 1) n = 1;
+    gm_kernel<BITS, GU><<<sms * n, kWarps * 32, 0, s>>>(*a, act, arows, lda, asum, ainv, ldg_s, *b, div, dst, ldd);
+    QE_CHECK(cudaGetLastError());
+    return 0;
 }
 
 }  // namespace
 
-/* Whether the grouped GEMVs cover this block: group size 64, 4- or 8-bit, every row a whole number of
- * 64-byte chunks (the gate/up rows at least kGuParts of them), 16-byte aligned activation rows. */
+/* Whether the grouped GEMVs cover this block: 4- or 8-bit codes in groups of 64, scales and biases in the
+ * [expert][group][row] layout, every matrix's rows a multiple of 8 (a tile's second 8 rows are whole). */
 bool qe_group_supported(const QeExpertArgs *a) {
     const int bits = a->gate.bits;
-    if (a->gate.group_size != kGS || (bits != 4 && bits != 8)) return false;
-    const int bh = a->hidden * bits / 8, bi = a->inter * bits / 8, bs = a->sh_inter * bits / 8;
-    return bh % kChunk == 0 && bh / kChunk >= kGuParts && bi % kChunk == 0 && bs % kChunk == 0 &&
-           a->inter % 4 == 0 && a->sh_inter % 4 == 0;
+    if ((bits != 4 && bits != 8) || a->gate.group_size != kGS) return false;
+    for (const QeQDev *q : {&a->gate, &a->up, &a->down, &a->sh_gate, &a->sh_up, &a->sh_down})
+        if (!q->scale_t || q->rows % 8 || q->cols % kGS || q->bits != bits || q->group_size != kGS) return false;
+    return true;
 }
 
-int qe_group_tokens(void) { return kNT; }
-int qe_group_rows(void) { return 32; }
+int qe_group_tokens(int /*bits*/) { return kTok; }
 
-/* CTAs of `kern` resident per SM with `smem` bytes of dynamic shared memory (at least 1). */
-static int resident(const void *kern, int threads, size_t smem) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, threads, smem) != cudaSuccess || n < 1) n = 1;
-    return n;
-}
-
-/* Gate/up + SwiGLU over the buckets (items: expert x 32-row tile x chunk of kNT tokens) -> h3 [pair][ldh].
- * A persistent grid of `sms` x resident CTAs walks the items (their count is on the device). */
-int qe_launch_group_gateup(const QeExpertArgs *a, const float *x, const QeBuckets *b, int sms, float *h3, int ldh,
-                           cudaStream_t s) {
+/* Gate/up + SwiGLU over the bucket's chunk list (bucket.cu with one tile per expert and chunks of kTok tokens),
+ * on x split by qe_launch_tc_prep (tb->act for T rows) -> h3 [pair][ldh] (fp32). */
+int qe_launch_group_gateup(const QeExpertArgs *a, const QeTcBufs *tb, int T, const QeBuckets *b, int sms, float *h3,
+                           int ldh, cudaStream_t s) {
     if (!qe_group_supported(a)) QE_FAIL("grouped gate/up: unsupported shape");
-    const size_t smem = sizeof(float) * (size_t)kNT * ((size_t)a->hidden + a->hidden / kGS);
-    const int threads = 2 * kGuParts * 32;
-    if (a->gate.bits == 4) {
-        const void *k = (const void *)group_gateup_kernel<4>;
-        QE_CHECK(qe_set_smem(k, smem));
-        group_gateup_kernel<4><<<sms * resident(k, threads, smem), threads, smem, s>>>(*a, x, *b, a->k + 1, h3, ldh);
-    } else {
-        const void *k = (const void *)group_gateup_kernel<8>;
-        QE_CHECK(qe_set_smem(k, smem));
-        group_gateup_kernel<8><<<sms * resident(k, threads, smem), threads, smem, s>>>(*a, x, *b, a->k + 1, h3, ldh);
-    }
-    QE_CHECK(cudaGetLastError());
-    return 0;
+    if (!b->chunks) QE_FAIL("grouped gate/up: no chunk list");
+    const int ng = a->hidden / kGS;
+    return a->gate.bits == 4
+               ? launch<4, true>(a, tb->act, T, a->hidden, tb->actsum, tb->actinv, ng, b, a->k + 1, h3, ldh, sms, s)
+               : launch<8, true>(a, tb->act, T, a->hidden, tb->actsum, tb->actinv, ng, b, a->k + 1, h3, ldh, sms, s);
 }
 
-/* Down projection over the buckets (items: expert x 32-row tile x chunk) -> ybuf [pair][hidden]. */
-int qe_launch_group_down(const QeExpertArgs *a, const float *h3, int ldh, const QeBuckets *b, int sms, float *ybuf,
-                         cudaStream_t s) {
+/* Down projection over the chunk list, on h3 split by qe_launch_split_rows (tb->h3s for npairs rows) ->
+ * ybuf [pair][hidden]. */
+int qe_launch_group_down(const QeExpertArgs *a, const QeTcBufs *tb, int npairs, const QeBuckets *b, int sms,
+                         float *ybuf, cudaStream_t s) {
     if (!qe_group_supported(a)) QE_FAIL("grouped down: unsupported shape");
-    const int K = a->inter > a->sh_inter ? a->inter : a->sh_inter;
-    const size_t smem = sizeof(float) * (size_t)kNT * ((size_t)K + K / kGS);
-    const int threads = kDnParts * 32;
-    if (a->gate.bits == 4) {
-        const void *k = (const void *)group_down_kernel<4>;
-        QE_CHECK(qe_set_smem(k, smem));
-        group_down_kernel<4><<<sms * resident(k, threads, smem), threads, smem, s>>>(*a, h3, ldh, *b, ybuf);
-    } else {
-        const void *k = (const void *)group_down_kernel<8>;
-        QE_CHECK(qe_set_smem(k, smem));
-        group_down_kernel<8><<<sms * resident(k, threads, smem), threads, smem, s>>>(*a, h3, ldh, *b, ybuf);
-    }
-    QE_CHECK(cudaGetLastError());
-    return 0;
+    if (!b->chunks) QE_FAIL("grouped down: no chunk list");
+    const int ng = tb->ldh / kGS;
+    return a->gate.bits == 4
+               ? launch<4, false>(a, tb->h3s, npairs, tb->ldh, tb->h3sum, tb->h3inv, ng, b, 1, ybuf, a->hidden, sms, s)
+               : launch<8, false>(a, tb->h3s, npairs, tb->ldh, tb->h3sum, tb->h3inv, ng, b, 1, ybuf, a->hidden, sms,
+                                  s);
 }

@@ -41,6 +41,8 @@ struct QeBuckets {
     int32_t *slot_expert; /* [E+1] active slots -> expert id (E = shared)     */
     int32_t *slot_items;  /* [2][E+2] per-slot work-item prefix, gate/up & down */
     int32_t *n_active;    /* [3]: active slots, gate/up items, down items     */
+    int4 *chunks;         /* [T*(k+1)] or null: with one tile per expert, chunk c of the gate/up item list as
+                             {expert, first bucket position, tokens} (the grouped GEMVs' work list) */
 };
 /* The shared expert's bucket holds rows [shared_first, shared_first + shared_tokens) of the batch. */
 int qe_launch_bucket(const int32_t *idx, int T, int E, int k, int shared_tokens, int tiles_gu, int tiles_sh_gu,
@@ -75,14 +77,6 @@ int qe_launch_decode_fused(const QeExpertArgs *a, const float *W, const float *b
                            int sms, cudaStream_t s);
 int qe_decode_error(void);
 int qe_decode_error_reset(void);
-/* Expert-centric grouped GEMVs for batched decode (group_gemv.cu). */
-bool qe_group_supported(const QeExpertArgs *a);
-int qe_group_tokens(void);
-int qe_group_rows(void);
-int qe_launch_group_gateup(const QeExpertArgs *a, const float *x, const QeBuckets *b, int sms, float *h3, int ldh,
-                           cudaStream_t s);
-int qe_launch_group_down(const QeExpertArgs *a, const float *h3, int ldh, const QeBuckets *b, int sms, float *ybuf,
-                         cudaStream_t s);
 int qe_launch_decode_gateup(const QeExpertArgs *a, const float *x, const int32_t *idx, int T, float *h3, int ldh,
                             cudaStream_t s);
 int qe_launch_decode_down_combine(const QeExpertArgs *a, const float *h3, int ldh, const int32_t *idx,
@@ -120,6 +114,16 @@ bool qe_tc_supported(const QeExpertArgs *a);
 size_t qe_tc_map_bytes(void);
 int qe_tc_weight_maps(const QeQDev *q, int n_experts, void *codes_map, void *sc_map, void *bi_map);
 int qe_launch_tc_prep(const QeExpertArgs *a, const float *x, int T, const QeTcBufs *tb, cudaStream_t s);
+int qe_launch_split_rows(int bits, const float *src, int K, int rows, __half *act, float *asum, float *ainv,
+                         cudaStream_t s);
+/* Expert-centric grouped GEMVs for batched decode (group_gemv.cu), on activations split as for the tcgen05
+ * kernels. */
+bool qe_group_supported(const QeExpertArgs *a);
+int qe_group_tokens(int bits);   /* tokens per chunk of the bucket lists the grouped GEMVs read */
+int qe_launch_group_gateup(const QeExpertArgs *a, const QeTcBufs *tb, int T, const QeBuckets *b, int sms, float *h3,
+                           int ldh, cudaStream_t s);
+int qe_launch_group_down(const QeExpertArgs *a, const QeTcBufs *tb, int npairs, const QeBuckets *b, int sms,
+                         float *ybuf, cudaStream_t s);
 int qe_launch_tc_gateup(const QeExpertArgs *a, const void *maps, const float *x, const QeBuckets *b, int T, int tn,
                         const QeTcBufs *t, int grid, cudaStream_t s);
 int qe_launch_tc_down(const QeExpertArgs *a, const void *maps, const QeBuckets *b, int T, int tn, const QeTcBufs *t,

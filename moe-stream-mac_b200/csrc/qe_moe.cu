@@ -28,11 +28,13 @@
 int qe_expert_rows_per_cta(int T);
 
 /* Expert path by batch size (auto): at most kDecodeMaxTokens tokens take the decode GEMVs (decode.cu); larger
- * batches the tensor-core (tcgen05) kernels when the shape allows (measured faster than the grouped GEMVs of
- * group_gemv.cu and the mma.sync kernels from 8 tokens up, on the 4-bit and 8-bit benchmark blocks); shapes
- * neither covers take the mma.sync kernels. The grouped GEMVs run when selected (QE_EXPERT_PATH=group). */
+ * batches with at most kGroupMaxPerExpert routed assignments per expert on average the grouped GEMVs
+ * (group_gemv.cu: measured faster than the tcgen05 kernels from 8 to 128 tokens on the 4-bit and 8-bit benchmark
+ * blocks, E=256, top-8); larger batches the tensor-core (tcgen05) kernels when the shape allows; shapes neither
+ * covers take the mma.sync kernels. QE_EXPERT_PATH=mma|tc|gemv|group forces one. */
 static constexpr int kTcMinTokens = 5;
 static constexpr int kDecodeMaxTokens = 4;
+static constexpr int kGroupMaxPerExpert = 4;
 
 /* ------------------------------------------------------------------ per-device context and workspace */
 
@@ -194,6 +196,7 @@ size_t scratch_layout(const QeMoeConfig &c, int T, char *base, Scratch *s) {
     t.b.slot_expert = (int32_t *)take(sizeof(int32_t) * (E + 2));
     t.b.slot_items = (int32_t *)take(sizeof(int32_t) * 2 * (E + 2));
     t.b.n_active = (int32_t *)take(sizeof(int32_t) * 4);
+    t.b.chunks = (int4 *)take(sizeof(int4) * npair);
     t.tcb.act = (__half *)take(2 * 2 * (size_t)T * c.hidden);
     t.tcb.actsum = (float *)take(4 * (size_t)T * (c.hidden / 64 + 1));
     t.tcb.actinv = (float *)take(4 * (size_t)T * (c.hidden / 64 + 1));
@@ -643,6 +646,16 @@ size_t qe_moe_weight_bytes(const QeMoe *m) { return m ? m->weight_bytes : 0; }
 
 namespace {
 
+/* The grouped GEMVs take a pass of T rows when selected (QE_EXPERT_PATH=group), or automatically when its routed
+ * assignments average at most kGroupMaxPerExpert per expert: there the expert stage is the weight stream, and the
+ * tensor-core tiles would spend a 32-token tile's conversion and epilogue on a few tokens. */
+bool group_path(const QeMoe *m, int T) {
+    if (!m->group) return false;
+    if (m->path == 4) return true;
+    return m->path == 0 && T > kDecodeMaxTokens &&
+           (long long)T * m->cfg.top_k <= (long long)kGroupMaxPerExpert * m->cfg.E;
+}
+
 /* Routing for one pass of T tokens: logits + idx/score in the scratch. */
 int run_route(QeMoe *m, const float *x, int T, Scratch &sc, cudaStream_t s) {
     const QeMoeConfig &c = m->cfg;
@@ -704,21 +717,23 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
         g_launches += 2;
         return 0;
     }
-    const bool use_group = m->group && m->path == 4;
+    const bool use_group = group_path(m, T);
     if (use_group) {
         /* batched decode: every active expert's rows streamed once per chunk of its tokens */
-        const int R = qe_group_rows(), NB = qe_group_tokens();
-        const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
-                  tiles_dn = (c.hidden + R - 1) / R;
-        if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s)) return -1;
+        const int np = T * (c.top_k + 1);
+        if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, 1, 1, 1, qe_group_tokens(c.bits), &sc.b, s) ||
+            qe_launch_tc_prep(&m->ex, x, T, &sc.tcb, s))
+            return -1;
         prof_mark(dev, s);
-        if (qe_launch_group_gateup(&m->ex, x, &sc.b, sms, sc.h3, I, s)) return -1;
-        prof_mark(dev, s);
-        if (qe_launch_group_down(&m->ex, sc.h3, I, &sc.b, sms, sc.ybuf, s)) return -1;
+        if (qe_launch_group_gateup(&m->ex, &sc.tcb, T, &sc.b, sms, sc.h3, I, s)) return -1;
+        prof_mark(dev, s);   /* the down stage includes the split of h3 */
+        if (qe_launch_split_rows(c.bits, sc.h3, I, np, sc.tcb.h3s, sc.tcb.h3sum, sc.tcb.h3inv, s) ||
+            qe_launch_group_down(&m->ex, &sc.tcb, np, &sc.b, sms, sc.ybuf, s))
+            return -1;
         prof_mark(dev, s);
         if (qe_launch_combine(sc.ybuf, sc.score, sc.logits, c.E + 1, T, c.E, c.top_k, c.hidden, out, s)) return -1;
         prof_mark(dev, s);
-        g_launches += 4;
+        g_launches += 6;
         return 0;
     }
     const bool use_tc = m->tc && (m->path == 2 || (m->path == 0 && T >= kTcMinTokens));
@@ -919,24 +934,26 @@ struct EpFold {
 
 /* The expert stages for n rows whose local slot ids and scores are in sc.idx / sc.score (and, for the shared
  * expert, whose gate logits are in sc.logits): bucket, gate/up + SwiGLU, down, then the selective combine
- * into out[n][hidden], or (scatter) into the home ranks' return buffers. */
-int run_experts(QeMoe *m, const float *x, float *out, int n, Scratch &sc, int sms, bool routed, bool shared,
+ * into out[n][hidden], or (scatter) into the home ranks' return buffers. q is the rows the path choice counts:
+ * the routed rows a rank receives (G x T in a token-sharded step), also for the shared-expert pass of T rows and
+ * for a folded pass, so that the shared expert takes the same kernels either way. */
+int run_experts(QeMoe *m, const float *x, float *out, int n, int q, Scratch &sc, int sms, bool routed, bool shared,
                 cudaStream_t s, const EpScatter *scatter = nullptr, const EpFold *fold = nullptr) {
     const QeMoeConfig &c = m->cfg;
     const int El = m->E_loc, k = c.top_k;
     const int I = c.inter > c.sh_inter ? c.inter : c.sh_inter;
     const int sh_tokens = fold ? fold->sh_n : shared ? n : 0, sh0 = fold ? fold->sh0 : 0;
-    const bool use_group = m->group && m->path == 4;
+    const bool use_group = group_path(m, q);
     const bool use_tc = !use_group && m->tc && (m->path == 2 || (m->path == 0 && n >= kTcMinTokens));
     if (use_group) {
-        const int R = qe_group_rows(), NB = qe_group_tokens();
-        const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
-                  tiles_dn = (c.hidden + R - 1) / R;
-        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, tiles_gu, tiles_sh, tiles_dn, NB, &sc.b, s, sh0) ||
-            qe_launch_group_gateup(&m->ex, x, &sc.b, sms, sc.h3, I, s) ||
-            qe_launch_group_down(&m->ex, sc.h3, I, &sc.b, sms, sc.ybuf, s))
+        const int np = n * (k + 1);
+        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, 1, 1, 1, qe_group_tokens(c.bits), &sc.b, s, sh0) ||
+            qe_launch_tc_prep(&m->ex, x, n, &sc.tcb, s) ||
+            qe_launch_group_gateup(&m->ex, &sc.tcb, n, &sc.b, sms, sc.h3, I, s) ||
+            qe_launch_split_rows(c.bits, sc.h3, I, np, sc.tcb.h3s, sc.tcb.h3sum, sc.tcb.h3inv, s) ||
+            qe_launch_group_down(&m->ex, &sc.tcb, np, &sc.b, sms, sc.ybuf, s))
             return -1;
-        g_launches += 3;
+        g_launches += 5;
     } else if (use_tc) {
         const int R = qe_tc_bm(), NB = m->tile ? m->tile : qe_tc_tokens_per_tile(n, c.top_k, c.E);
         const int tiles_gu = (c.inter + R - 1) / R, tiles_sh = (c.sh_inter + R - 1) / R,
@@ -1351,7 +1368,9 @@ int qe_moe_ep_route_device(QeMoe *m, int T, const float *x, int32_t *meta, float
         ep_meta_kernel<<<(n * k + 255) / 256, 256, 0, s>>>(sc.idx, sc.score, n, k, meta + (size_t)t0 * 2 * k);
         QE_CHECK(cudaGetLastError());
         QE_CHECK(cudaMemsetAsync(sc.idx, 0xff, sizeof(int32_t) * (size_t)n * k, s));   /* shared expert only */
-        if (run_experts(m, x + (size_t)t0 * H, shared + (size_t)t0 * H, n, sc, d->sms, false, true, s)) return -1;
+        if (run_experts(m, x + (size_t)t0 * H, shared + (size_t)t0 * H, n, n * m->cfg.ep_size, sc, d->sms, false, true,
+                        s))
+            return -1;
         g_launches += 1;   /* ep_meta_kernel */
     }
     return 0;
@@ -1390,7 +1409,7 @@ int qe_moe_ep_experts_device(QeMoe *m, int n, const float *x, const int32_t *met
         ep_local_kernel<<<(cnt * k + 255) / 256, 256, 0, s>>>(meta + (size_t)r0 * 2 * k, cnt, k, m->cfg.ep_rank,
                                                              place_of(m), sc.idx, sc.score);
         QE_CHECK(cudaGetLastError());
-        if (run_experts(m, x + (size_t)r0 * H, partial + (size_t)r0 * H, cnt, sc, d->sms, true, false, s)) return -1;
+        if (run_experts(m, x + (size_t)r0 * H, partial + (size_t)r0 * H, cnt, cnt, sc, d->sms, true, false, s)) return -1;
         g_launches += 1;
     }
     return 0;
@@ -1651,7 +1670,7 @@ int qe_moe_ep_experts_p2p(QeMoe *m, QeEpXchg *xc, int T, void *stream) {
         const EpScatter sca = {(float *const *)(xc->dptr + 2 * G), r0, T, m->cfg.ep_rank};
         const int o0 = r0 + cr - nr;                          /* first own row of this pass */
         const EpFold fo = {cr, cnt - cr, gate + std::max(0, o0), sh_out + (size_t)std::max(0, o0) * H};
-        if (run_experts(m, rx + (size_t)r0 * H, nullptr, cnt, sc, d->sms, true, false, s, &sca,
+        if (run_experts(m, rx + (size_t)r0 * H, nullptr, cnt, fold ? cr : cnt, sc, d->sms, true, false, s, &sca,
                         fold ? &fo : nullptr))
             return -1;
     }

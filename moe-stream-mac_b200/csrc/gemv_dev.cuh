@@ -1,4 +1,4 @@
-/* gemv_dev.cuh: lane-level helpers shared by the CUDA-core GEMVs (decode.cu, group_gemv.cu).
+/* gemv_dev.cuh: lane-level helpers of the coalesced CUDA-core GEMVs (decode.cu).
  *
  * Codes follow the MLX affine layout of the reference (engine/src/qgroup.c: code j of a group at bit
  * (j % (32/bits))*bits of word j / (32/bits), LSB first).
@@ -57,8 +57,5 @@ __device__ __forceinline__ float dg_reduce(float (&v)[J], int lane) {
     }
     return v[0];
 }
-
-/* dg_reduce leaves J / LPR values per lane when J > LPR: v[0 .. J/LPR - 1] are the sums of loads
- * dg_index<LPR, J>(lane) + i. */
 
 #endif

@@ -234,7 +234,7 @@ bool qe_group_supported(const QeExpertArgs *a) {
     return true;
 }
 
-int qe_group_tokens(int /*bits*/) { return kTok; }
+int qe_group_tokens(void) { return kTok; }
 
 /* Gate/up + SwiGLU over the bucket's chunk list (bucket.cu with one tile per expert and chunks of kTok tokens),
  * on x split by qe_launch_tc_prep (tb->act for T rows) -> h3 [pair][ldh] (fp32). */

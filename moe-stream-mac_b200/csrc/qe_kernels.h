@@ -119,7 +119,7 @@ int qe_launch_split_rows(int bits, const float *src, int K, int rows, __half *ac
 /* Expert-centric grouped GEMVs for batched decode (group_gemv.cu), on activations split as for the tcgen05
  * kernels. */
 bool qe_group_supported(const QeExpertArgs *a);
-int qe_group_tokens(int bits);   /* tokens per chunk of the bucket lists the grouped GEMVs read */
+int qe_group_tokens(void);   /* tokens per chunk of the bucket lists the grouped GEMVs read */
 int qe_launch_group_gateup(const QeExpertArgs *a, const QeTcBufs *tb, int T, const QeBuckets *b, int sms, float *h3,
                            int ldh, cudaStream_t s);
 int qe_launch_group_down(const QeExpertArgs *a, const QeTcBufs *tb, int npairs, const QeBuckets *b, int sms,

@@ -721,7 +721,7 @@ int run_pass(QeMoe *m, const float *x, float *out, int T, Scratch &sc, int sms, 
     if (use_group) {
         /* batched decode: every active expert's rows streamed once per chunk of its tokens */
         const int np = T * (c.top_k + 1);
-        if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, 1, 1, 1, qe_group_tokens(c.bits), &sc.b, s) ||
+        if (qe_launch_bucket(sc.idx, T, c.E, c.top_k, T, 1, 1, 1, qe_group_tokens(), &sc.b, s) ||
             qe_launch_tc_prep(&m->ex, x, T, &sc.tcb, s))
             return -1;
         prof_mark(dev, s);
@@ -947,7 +947,7 @@ int run_experts(QeMoe *m, const float *x, float *out, int n, int q, Scratch &sc,
     const bool use_tc = !use_group && m->tc && (m->path == 2 || (m->path == 0 && n >= kTcMinTokens));
     if (use_group) {
         const int np = n * (k + 1);
-        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, 1, 1, 1, qe_group_tokens(c.bits), &sc.b, s, sh0) ||
+        if (qe_launch_bucket(sc.idx, n, El, k, sh_tokens, 1, 1, 1, qe_group_tokens(), &sc.b, s, sh0) ||
             qe_launch_tc_prep(&m->ex, x, n, &sc.tcb, s) ||
             qe_launch_group_gateup(&m->ex, &sc.tcb, n, &sc.b, sms, sc.h3, I, s) ||
             qe_launch_split_rows(c.bits, sc.h3, I, np, sc.tcb.h3s, sc.tcb.h3sum, sc.tcb.h3inv, s) ||

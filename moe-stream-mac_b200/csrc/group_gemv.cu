@@ -27,6 +27,8 @@
  *   down       y -> ybuf[pair][row], summed per token by the combine kernel in slot order (moe_layer.c:79-88)
  * The next group's codes, activations, scales and biases are loaded while this group's MMAs run.
  */
+#include <atomic>
+
 #include "qe_common.cuh"
 #include "qe_kernels.h"
 
@@ -214,9 +216,16 @@ __global__ void __launch_bounds__(kWarps * 32) gm_kernel(QeExpertArgs a, const _
 template <int BITS, bool GU>
 int launch(const QeExpertArgs *a, const __half *act, int arows, int lda, const float *asum, const float *ainv,
            int ldg_s, const QeBuckets *b, int div, float *dst, int ldd, int sms, cudaStream_t s) {
-    const void *k = (const void *)gm_kernel<BITS, GU>;
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k, kWarps * 32, 0) != cudaSuccess || n < 1) n = 1;
+    /* resident CTAs per SM, queried once per kernel (the same on every B200): a decode step cannot afford the
+     * query's host time on every launch */
+    static std::atomic<int> resident{0};
+    int n = resident.load(std::memory_order_relaxed);
+    if (n == 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, (const void *)gm_kernel<BITS, GU>, kWarps * 32, 0) !=
+                cudaSuccess || n < 1)
+            n = 1;
+        resident.store(n, std::memory_order_relaxed);
+    }
     gm_kernel<BITS, GU><<<sms * n, kWarps * 32, 0, s>>>(*a, act, arows, lda, asum, ainv, ldg_s, *b, div, dst, ldd);
     QE_CHECK(cudaGetLastError());
     return 0;
